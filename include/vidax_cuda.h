@@ -1,0 +1,81 @@
+/*
+ * vidax_cuda.h -- C ABI of libvidax_cuda.so, the B200 (sm_100a) implementation
+ * of vidax's attention hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and element strides
+ * and a CUDA stream; none allocates or frees caller memory, none synchronises
+ * the host. Return value: VX_OK or a VX_E* code; vx_last_error() gives the
+ * message of the last failure on the calling thread.
+ *
+ * Layouts follow vidax: attention tensors are BSHD (batch, seq, heads,
+ * head_dim) with head_dim contiguous; neighborhood tensors are
+ * (B, T, H, W, heads, head_dim). Element type bf16 in and out, fp32 softmax.
+ */
+#ifndef VIDAX_CUDA_H_
+#define VIDAX_CUDA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* vx_stream_t;
+
+enum {
+  VX_OK = 0,
+  VX_EINVAL = 1,        /* bad argument: shape, stride, alignment, null pointer */
+  VX_EUNSUPPORTED = 2,  /* valid request this build does not implement */
+  VX_ECUDA = 3,         /* CUDA runtime / driver error */
+  VX_ENCCL = 4,         /* NCCL error */
+  VX_ETIMEOUT = 5,      /* a bounded device-side wait expired (see vx_device_status) */
+};
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int vx_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* vx_last_error(void);
+
+/*
+ * Reads (and optionally clears) the device status word of the current CUDA
+ * device: 0 when every kernel ran to completion, else an OR of
+ * 1 (load wait timed out), 2 (MMA wait), 4 (softmax wait), 8 (drain).
+ * Synchronises the device. Returns VX_OK or VX_ECUDA.
+ */
+int vx_device_status(int* status_out, int clear);
+
+/* ----------------------------------------------------------------------
+ * Full (non-causal) attention:  o = softmax(scale * q k^T) v   per (b, h).
+ *
+ * Replaces the kernel call behind vidax.core.attention.dot_product_attention
+ * (src/vidax/core/attention.py:467-533), local_attention (:321-338) and the
+ * per-device flash call inside _flash_attention_tpu (:212-288): the Pallas
+ * flash_attention / splash_attention custom calls on TPU and
+ * jax.nn.dot_product_attention elsewhere. Key padding (the SegmentIds mask at
+ * attention.py:272-278 and the Hunyuan key-valid mask,
+ * src/vidax/models/hunyuan_video/common/dit_layers.py:150-191) is expressed
+ * as kv_len: keys at index >= kv_len[b] are invisible.
+ */
+typedef struct vx_attn_args {
+  const void* q;  /* (B, Sq, Hq, D) bf16 */
+  const void* k;  /* (B, Sk, Hkv, D) bf16 */
+  const void* v;  /* (B, Sk, Hkv, D) bf16 */
+  void* o;        /* (B, Sq, Hq, D) bf16 */
+  int64_t q_stride[3]; /* element strides of dims (b, s, h); d stride must be 1 */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int32_t batch, seq_q, seq_k, heads_q, heads_kv, head_dim;
+  float scale;             /* softmax scale, > 0 */
+  const int32_t* kv_len;   /* optional device int32[B]; NULL = all seq_k keys valid */
+  float* lse;              /* optional device fp32 (B, Hq, Sq): natural-log sum-exp */
+} vx_attn_args;
+
+int vx_attn_fwd(const vx_attn_args* args, vx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VIDAX_CUDA_H_ */

@@ -1,0 +1,440 @@
+// Warp-specialised tcgen05/TMEM attention forward for sm_100a (head_dim 128,
+// bf16 in/out, fp32 softmax and accumulation).
+//
+// One CTA owns a pair of 128-row query tiles (Q0, Q1) of one (batch, head)
+// and streams 128-key K/V tiles through a two-stage TMA ring:
+//
+//   warps 0-3  softmax warpgroup for Q0   (thread i owns query row i)
+//   warps 4-7  softmax warpgroup for Q1
+//   warp  8    TMA producer (one elected lane)
+//   warp  9    TMEM allocator + MMA issuer (one elected lane)
+//
+// Tensor memory (512 columns x 128 lanes, fp32):
+//   [  0,128) S0 = Q0 K^T   (P0 = softmax numerators, bf16, aliases cols [0,64))
+//   [128,256) S1 = Q1 K^T   (P1 aliases cols [128,192))
+//   [256,384) O0 += P0 V
+//   [384,512) O1 += P1 V
+//
+// MMA order per KV tile j (ping-pong so the tensor core works on one query
+// tile while the other one's softmax runs):
+//   PV0(j) ; S0(j+1) ; PV1(j) ; S1(j+1)
+// S0(j+1) overwrites the columns PV0(j) reads P0 from; tcgen05.mma ops issued
+// by one thread execute in issue order, which orders that reuse.
+//
+// Online softmax uses a lazy rescale: the running row maximum used in the
+// exponent only moves when the new maximum exceeds it by more than
+// kRescaleThreshold (log2 units), so the O accumulator in TMEM is rescaled
+// rarely; P values stay <= 2^kRescaleThreshold, well inside bf16 range. The
+// final O / l is exact regardless of which maximum was used.
+//
+// The geometry policy (`Geo`) decides which rows form the query tiles, which
+// K/V tiles are visited, how keys are masked and where output rows go: the
+// dense policy serves full attention, the neighborhood policy serves 3-D
+// windowed attention with the same pipeline.
+#pragma once
+
+#include "sm100_common.cuh"
+
+namespace vx {
+namespace attn {
+
+constexpr int kHeadDim = 128;
+constexpr int kBlockM = 128;  // query rows per tile (one softmax warpgroup)
+constexpr int kBlockN = 128;  // keys per K/V tile
+constexpr int kStages = 2;
+constexpr int kThreads = 320;
+constexpr uint32_t kTileBytes = 128u * 128u * 2u;  // one 128x128 bf16 tile
+constexpr uint32_t kHalfBytes = kTileBytes / 2;     // 128 rows x 64 cols (128B rows)
+constexpr float kRescaleThreshold = 8.0f;
+
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
+constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
+constexpr uint32_t kSmemBar = kSmemV + kStages * kTileBytes;
+constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + barriers + alignment slack
+
+// barrier slots
+enum : int {
+  kQFull = 0,      // 2
+  kKFull = 2,      // kStages
+  kKEmpty = 4,     // kStages
+  kVFull = 6,      // kStages
+  kVEmpty = 8,     // kStages
+  kSFull = 10,     // 2
+  kPFull = 12,     // 2
+  kOFull = 14,     // 2
+  kDrain = 16,     // 1
+  kNumBars = 17,
+};
+constexpr uint32_t kTmemSlotOff = kSmemBar + 8 * kNumBars;
+constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
+constexpr uint32_t kScratchOff = kAbortOff + 4;  // 16 ints of per-CTA scratch
+
+constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false, false);  // Q K^T: both K-major
+constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, false, true);   // P V : V is N-major
+
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
+// S_t = Q_t K^T over head_dim 128 (8 MMAs of K=16). Each operand tile is two
+// 128B-swizzled halves of 64 columns; within a half the K step advances the
+// descriptor start address by 32 bytes.
+__device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_smem, uint32_t k_smem) {
+#pragma unroll
+  for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+    mma_ss(tmem_s, sdesc_sw128(q_smem + off, 16, 1024), sdesc_sw128(k_smem + off, 16, 1024),
+           kIdescS, kk > 0 ? 1u : 0u);
+  }
+}
+
+// O_t (+)= P_t V with P_t read from tensor memory (8 columns per K=16 step)
+// and V an N-major 128B-swizzled tile: 16 keys per step = 2048 bytes; the two
+// 64-column halves of head_dim are kHalfBytes apart (leading byte offset).
+__device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_smem,
+                                         bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < kBlockN / 16; ++kk) {
+    mma_ts(tmem_o, tmem_p + kk * 8, sdesc_sw128(v_smem + kk * 2048, kHalfBytes, 1024), kIdescO,
+           (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void pin32(uint32_t (&r)[32]) { asm volatile("" : VX_RW32(r)); }
+
+template <class Geo>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                    const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ typename Geo::Params p) {
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) -> uint32_t { return sbase + kSmemBar + 8u * i; };
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kTmemSlotOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
+  int* status = p.status;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  Geo geo(p, reinterpret_cast<int*>(smem + kScratchOff));
+  const int n_kv = geo.num_kv_tiles();
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kQFull + 0), 1);
+    mbar_init(bar(kQFull + 1), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kKFull + s), 1);
+      mbar_init(bar(kKEmpty + s), 1);
+      mbar_init(bar(kVFull + s), 1);
+      mbar_init(bar(kVEmpty + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kSFull + t), 1);
+      mbar_init(bar(kPFull + t), 128);
+      mbar_init(bar(kOFull + t), 1);
+    }
+    mbar_init(bar(kDrain), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(sbase + kTmemSlotOff, 512);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_kv > 0) {
+      const uint64_t pol_q = l2_policy_evict_first();
+      const uint64_t pol_kv = l2_policy_evict_last();
+      for (int t = 0; t < 2; ++t) {
+        mbar_expect_tx(bar(kQFull + t), kTileBytes);
+        geo.load_q(&tm_q, t, sbase + kSmemQ + t * kTileBytes, bar(kQFull + t), pol_q);
+      }
+      int jk = -1, jv = -1;  // last K / V tile whose load was issued
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!mbar_wait(bar(kKEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) break;
+        mbar_expect_tx(bar(kKFull + s), kTileBytes);
+        geo.load_kv(&tm_k, j, sbase + kSmemK + s * kTileBytes, bar(kKFull + s), pol_kv);
+        jk = j;
+        if (!mbar_wait(bar(kVEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) break;
+        mbar_expect_tx(bar(kVFull + s), kTileBytes);
+        geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kVFull + s), pol_kv);
+        jv = j;
+      }
+      if (*abort_flag) {
+        // Drain: wait for the most recent load into each stage to land so no
+        // TMA write targets this CTA's shared memory after it exits. Only the
+        // last load per stage can still be pending, so its parity is exact.
+        for (int j = jk; j >= 0 && j > jk - kStages; --j)
+          mbar_wait_drain(bar(kKFull + j % kStages), (j / kStages) & 1, status);
+        for (int j = jv; j >= 0 && j > jv - kStages; --j)
+          mbar_wait_drain(bar(kVFull + j % kStages), (j / kStages) & 1, status);
+        mbar_wait_drain(bar(kQFull + 0), 0, status);
+        mbar_wait_drain(bar(kQFull + 1), 0, status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_kv > 0) {
+      const uint32_t q0 = sbase + kSmemQ, q1 = sbase + kSmemQ + kTileBytes;
+      const uint32_t t_s0 = tmem, t_s1 = tmem + 128, t_o0 = tmem + 256, t_o1 = tmem + 384;
+      bool ok = mbar_wait(bar(kQFull + 0), 0, abort_flag, status, kDevTimeoutMma) &&
+                mbar_wait(bar(kKFull + 0), 0, abort_flag, status, kDevTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(t_s0, q0, sbase + kSmemK);
+        tc_commit(bar(kSFull + 0));
+      }
+      ok = ok && mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(t_s1, q1, sbase + kSmemK);
+        tc_commit(bar(kSFull + 1));
+        tc_commit(bar(kKEmpty + 0));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int s1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
+        const bool has_next = j + 1 < n_kv;
+        const uint32_t v_sm = sbase + kSmemV + s * kTileBytes;
+        const uint32_t k_next = sbase + kSmemK + s1 * kTileBytes;
+        if (!mbar_wait(bar(kVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
+        if (!mbar_wait(bar(kPFull + 0), j & 1, abort_flag, status, kDevTimeoutMma)) break;
+        tc_fence_after();
+        issue_pv(t_o0, t_s0, v_sm, j > 0);
+        if (!has_next) tc_commit(bar(kOFull + 0));
+        if (has_next) {
+          if (!mbar_wait(bar(kKFull + s1), ph1, abort_flag, status, kDevTimeoutMma)) break;
+          tc_fence_after();
+          issue_qk(t_s0, q0, k_next);
+          tc_commit(bar(kSFull + 0));
+        }
+        if (!mbar_wait(bar(kPFull + 1), j & 1, abort_flag, status, kDevTimeoutMma)) break;
+        tc_fence_after();
+        issue_pv(t_o1, t_s1, v_sm, j > 0);
+        tc_commit(bar(kVEmpty + s));
+        if (!has_next) tc_commit(bar(kOFull + 1));
+        if (has_next) {
+          issue_qk(t_s1, q1, k_next);
+          tc_commit(bar(kSFull + 1));
+          tc_commit(bar(kKEmpty + s1));
+        }
+      }
+      // Drain: no MMA may still be running when TMEM is released.
+      tc_commit(bar(kDrain));
+      mbar_wait_drain(bar(kDrain), 0, status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int wg = warp >> 2;    // which query tile
+    const int quad = warp & 3;   // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t t_s = tmem + wg * 128 + lane_off;
+    const uint32_t t_o = tmem + 256 + wg * 128 + lane_off;
+    const float scale_log2 = p.scale_log2;
+    geo.softmax_setup(wg, row);
+
+    float m_used = neg_inf();
+    float l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      ok = mbar_wait(bar(kSFull + wg), j & 1, abort_flag, status, kDevTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sr[c]);
+      tmem_wait_ld_only();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) pin32(sr[c]);
+
+      geo.mask_scores(j, sr);
+
+      float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          mx0 = fmaxf(mx0, __uint_as_float(sr[c][i + 0]));
+          mx1 = fmaxf(mx1, __uint_as_float(sr[c][i + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(sr[c][i + 2]));
+          mx3 = fmaxf(mx3, __uint_as_float(sr[c][i + 3]));
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale_log2;
+      const float m_new = fmaxf(m_used, mx);
+      const bool need = m_new > m_used + kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) alpha = ex2_approx(m_used - m_new);  // 0 when m_used = -inf
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O(j-1) is complete: S(j) was issued after PV(j-1) and its commit
+        // tracks every earlier MMA. Rescale this warp's 32 rows of O.
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(t_o + c * 32, orr);
+          tmem_wait_ld(orr);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+          tmem_st32(t_o + c * 32, orr);
+        }
+      }
+      if (need) {
+        l_sum *= alpha;
+        m_used = m_new;
+      }
+      const float neg_m = (m_used == neg_inf()) ? 0.f : -m_used;
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m));
+          const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m));
+          ls0 += e0;
+          ls1 += e1;
+          pk[i] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(t_s + c * 16, pk);
+      }
+      l_sum += ls0 + ls1;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(kPFull + wg));
+    }
+
+    if (n_kv == 0) {
+      geo.store_zero_row(wg, row);
+    } else if (ok) {
+      ok = mbar_wait(bar(kOFull + wg), 0, abort_flag, status, kDevTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(t_o + c * 32, orr);
+          tmem_wait_ld(orr);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(__uint_as_float(orr[2 * i]) * inv_l,
+                                __uint_as_float(orr[2 * i + 1]) * inv_l);
+          geo.store_row_chunk(wg, row, c, pk);
+        }
+        // natural-log LSE of the row's scaled logits
+        const float lse = l_sum > 0.f ? (m_used + __log2f(l_sum)) * 0.69314718055994531f
+                                      : neg_inf();
+        geo.store_lse(wg, row, lse);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Dense geometry: query tiles are consecutive rows of one (batch, head); the
+// K/V tiles sweep all valid keys; keys at index >= kv_valid are masked.
+// Tensors are BSHD; the tensor maps are 4-D {D, H, S, B}.
+struct DenseParams {
+  __nv_bfloat16* o;
+  long long o_sb, o_ss, o_sh;  // output strides in elements (d stride is 1)
+  float* lse;                  // optional (B, H, Sq) fp32
+  const int* kv_len;           // optional [B]
+  int* status;
+  int B, Sq, Sk, H, Hkv;
+  float scale_log2;
+};
+
+struct DenseGeo {
+  using Params = DenseParams;
+  const DenseParams& p;
+  int b, h, hk, q0, kv_valid;
+  int row_global;
+
+  __device__ DenseGeo(const DenseParams& prm, int*) : p(prm) {
+    q0 = blockIdx.x * (2 * kBlockM);
+    h = blockIdx.y;
+    b = blockIdx.z;
+    hk = h / (p.H / p.Hkv);
+    int kv = p.Sk;
+    if (p.kv_len != nullptr) kv = min(max(p.kv_len[b], 0), p.Sk);
+    kv_valid = kv;
+  }
+  __device__ int num_kv_tiles() const { return (kv_valid + kBlockN - 1) / kBlockN; }
+  __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
+                         uint64_t pol) const {
+    tma_load_4d(dst, tm, bar, 0, h, q0 + t * kBlockM, b, pol);
+    tma_load_4d(dst + kHalfBytes, tm, bar, 64, h, q0 + t * kBlockM, b, pol);
+  }
+  __device__ void load_kv(const CUtensorMap* tm, int j, uint32_t dst, uint32_t bar,
+                          uint64_t pol) const {
+    tma_load_4d(dst, tm, bar, 0, hk, j * kBlockN, b, pol);
+    tma_load_4d(dst + kHalfBytes, tm, bar, 64, hk, j * kBlockN, b, pol);
+  }
+  __device__ void softmax_setup(int wg, int row) { row_global = q0 + wg * kBlockM + row; }
+  __device__ void mask_scores(int j, uint32_t (&sr)[4][32]) const {
+    const int rem = kv_valid - j * kBlockN;
+    if (rem < kBlockN) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i >= rem) sr[c][i] = 0xff800000u;
+    }
+  }
+  __device__ __nv_bfloat16* row_ptr() const {
+    return p.o + b * p.o_sb + static_cast<long long>(row_global) * p.o_ss + h * p.o_sh;
+  }
+  __device__ void store_row_chunk(int, int, int c, const uint32_t (&pk)[16]) const {
+    if (row_global >= p.Sq) return;
+    uint4* dst = reinterpret_cast<uint4*>(row_ptr() + c * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+  }
+  __device__ void store_zero_row(int, int) const {
+    if (row_global >= p.Sq) return;
+    uint4* dst = reinterpret_cast<uint4*>(row_ptr());
+#pragma unroll
+    for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+    if (p.lse != nullptr)
+      p.lse[(static_cast<long long>(b) * p.H + h) * p.Sq + row_global] = neg_inf();
+  }
+  __device__ void store_lse(int, int, float lse) const {
+    if (p.lse == nullptr || row_global >= p.Sq) return;
+    p.lse[(static_cast<long long>(b) * p.H + h) * p.Sq + row_global] = lse;
+  }
+};
+
+}  // namespace attn
+}  // namespace vx
