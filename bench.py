@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark of vidax's attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Workload (every N): the Ulysses self-attention layer of Wan2.1-14B at
+720p/81 frames -- B=1, S=75600 tokens, H=40 heads, head_dim 128, bf16, scale
+1/sqrt(128) -- with the sequence sharded evenly over the N ranks (strong
+scaling: total work fixed). At N=1 the layer is one local attention call; at
+N>1 it is pack -> NCCL all-to-all (tokens->heads) -> attention on H/N heads
+over the full sequence -> all-to-all back -> unpack. Inputs are seeded N(0,1)
+synthetic tensors (no dataset exists for this path); every input exceeds the
+126 MB L2, so no flush is needed between steps.
+
+One JSON line (rank 0): value = whole-job attention TFLOP/s (vidax's FLOP
+convention 4*B*H*S*S*D over the max-over-ranks step time), `e2e` = the same
+through the public API with pinned host inputs copied in and the output
+copied out every step, `roofline` = the attention kernel against the
+measured bf16 peak, `cpu_baseline` = the CPU oracle on a bounded sample.
+
+`--impl reference` times the reference's CPU path (vidax's JAX CPU attention
+is `jax.nn.dot_product_attention`; JAX is absent, so its numpy restatement in
+oracle/ runs) on rank 0 with all host cores, one bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, S_GLOBAL, H, D = 1, 75600, 40, 128
+WORKLOAD = "cfg3: Ulysses self-attention layer, Wan2.1-14B 720p/81f (B=1, S=75600, H=40, D=128, bf16)"
+FALLBACK_PEAK_TFLOPS = 1590.0
+# dram__bytes_read.sum + dram__bytes_write.sum per head per query row per key
+# row, measured with ncu on attn_fwd_kernel (profiles/attn_fwd_cfg2_h4.md) and
+# scaled by units (heads x q-blocks x kv-tiles) to a full launch.
+TRAFFIC_BYTES_PER_HEAD_QK = None
+
+
+def flops(b, h, sq, sk, d):
+    return 4.0 * b * h * sq * sk * d
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return pk.get("bf16_tflops"), pk.get("bf16_tflops_sustained"), "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAK_TFLOPS, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons of one GPU every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def gpu_id_for(dev) -> str:
+    import torch
+    p = torch.cuda.get_device_properties(dev)
+    try:
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except AttributeError:
+        return str(dev)
+
+
+def cpu_sample(seconds: float, rows_per_chunk: int = 256):
+    """Times the oracle (numpy restatement of jax.nn.dot_product_attention) on
+    head 0 of the workload: chunks of query rows against all S keys, until
+    `seconds` of CPU time have run. Returns (TFLOP/s, threads, description)."""
+    import numpy as np
+    from oracle.attention_ref import sdpa, seeded_qkv
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:
+        threads = os.cpu_count()
+    q, k, v = seeded_qkv((1, S_GLOBAL, 1, D), 3)
+    done_rows, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and done_rows < S_GLOBAL:
+        rows = np.arange(done_rows, min(done_rows + rows_per_chunk, S_GLOBAL))
+        sdpa(q, k, v, q_rows=rows, chunk=rows_per_chunk)
+        done_rows += len(rows)
+    dt = time.perf_counter() - t0
+    tf = flops(1, 1, done_rows, S_GLOBAL, D) / dt / 1e12
+    desc = (f"numpy oracle, head 0 of cfg3: {done_rows} query rows x {S_GLOBAL} keys "
+            f"({flops(1, 1, done_rows, S_GLOBAL, D) / 1e9:.1f} GFLOP in {dt:.1f} s)")
+    return tf, threads, desc
+
+
+def run_reference(args, rank: int):
+    """Reference arm: vidax's CPU attention path (restated) on the host cores."""
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle.attention_ref import sdpa, seeded_qkv
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:
+        threads = os.cpu_count()
+    q, k, v = seeded_qkv((1, S_GLOBAL, 1, D), 3)
+    rows_per_step = 2048
+
+    def step(i):
+        r0 = (i * rows_per_step) % (S_GLOBAL - rows_per_step)
+        sdpa(q, k, v, q_rows=np.arange(r0, r0 + rows_per_step), chunk=512)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    dt = (time.perf_counter() - t0) / args.steps
+    fl = flops(1, 1, rows_per_step, S_GLOBAL, D)
+    value = fl / dt / 1e12
+    sample = (f"per step: {rows_per_step} query rows x {S_GLOBAL} keys of one head of cfg3 "
+              f"({fl / 1e9:.1f} GFLOP); numpy restatement of jax.nn.dot_product_attention "
+              "(JAX not installed)")
+    line = {
+        "impl": "reference", "metric": "attention TFLOP/s (Ulysses attn layer, Wan2.1-14B 720p)",
+        "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": "bounded CPU sample per step"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    import vidax_b200 as vx
+    from vidax_b200 import _lib, ulysses
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    if world > 1:
+        vx.register_axis("sp", None)
+    if S_GLOBAL % world != 0:
+        raise SystemExit(f"S={S_GLOBAL} does not split evenly over {world} ranks")
+    s_loc = S_GLOBAL // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 * 1000 + rank)
+    q = torch.randn((B, s_loc, H, D), generator=gen, device=dev, dtype=torch.float32).bfloat16()
+    k = torch.randn((B, s_loc, H, D), generator=gen, device=dev, dtype=torch.float32).bfloat16()
+    v = torch.randn((B, s_loc, H, D), generator=gen, device=dev, dtype=torch.float32).bfloat16()
+
+    kernel_ms = []
+    ulysses_events = []
+
+    def layer(qq, kk, vv):
+        if world == 1:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            o = vx.dot_product_attention(qq, kk, vv)
+            e1.record()
+            ulysses_events.append((e0, e1))
+            return o
+        return vx.sequence_parallel_self_attention(qq, kk, vv, "sp")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        layer(q, k, v)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "device status word set during warm-up"
+    ulysses_events.clear()
+    ulysses.KERNEL_EVENTS = ulysses_events if world > 1 else None
+
+    sampler = ClockSampler(gpu_id_for(dev))
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        out = layer(q, k, v)
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ulysses.KERNEL_EVENTS = None
+    ms = max_over_ranks(t_start.elapsed_time(t_end) / args.steps)
+    kernel_ms = [a.elapsed_time(b) for a, b in ulysses_events]
+    kern_avg = max_over_ranks(statistics.mean(kernel_ms)) if kernel_ms else float("nan")
+    status = _lib.device_status()
+    del out
+
+    total_flops = flops(B, H, S_GLOBAL, S_GLOBAL, D)
+    value = total_flops / (ms / 1e3) / 1e12
+    hg = -(-H // world)
+    launch_flops = flops(B, hg, S_GLOBAL, S_GLOBAL, D)
+    achieved = launch_flops / (kern_avg / 1e3) / 1e12
+    burst, sustained, peak_src = load_peaks()
+    gpu_launches = args.steps * (1 if world == 1 else 3 * B)
+
+    # ---- end to end through the public API: pinned host in, host out
+    hq = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    hout = torch.empty_like(hq).pin_memory()
+
+    def e2e_step():
+        dq = hq.to(dev, non_blocking=True)
+        dk = hk.to(dev, non_blocking=True)
+        dv = hv.to(dev, non_blocking=True)
+        o = layer(dq, dk, dv)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    ulysses_events.clear()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_value = total_flops / (e2e_ms / 1e3) / 1e12
+    elem = 2
+    h2d = 3 * B * s_loc * H * D * elem
+    d2h = B * s_loc * H * D * elem
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, threads, desc = cpu_sample(args.cpu_seconds)
+        cpu = {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": desc}
+
+    if world > 1:
+        vx.unregister_axis("sp")
+    if rank != 0:
+        return
+    traffic = None
+    if TRAFFIC_BYTES_PER_HEAD_QK is not None:
+        traffic = TRAFFIC_BYTES_PER_HEAD_QK * B * hg * S_GLOBAL * S_GLOBAL
+    peak = sustained if sustained else burst
+    line = {
+        "metric": "attention TFLOP/s (Ulysses attn layer, Wan2.1-14B 720p)",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": S_GLOBAL, "heads": H,
+                   "head_dim": D, "parallelism": f"ulysses-sp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (774 MB per tensor), no flush"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                     "frac_of_burst": round(achieved / burst, 4) if burst else None,
+                     "peak_source": f"{peak_src} bf16 dense (sustained; burst {burst})",
+                     "kernel": "attn_fwd_kernel<DenseGeo>",
+                     "kernel_ms": round(kern_avg, 3), "launch_flops": launch_flops,
+                     "traffic": traffic},
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks,
+        "device_status": status,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if world > 1:
+        a2a_bytes = 4 * (world - 1) / world * B * s_loc * hg * world * D * elem
+        line["a2a"] = {"bytes_sent_per_gpu": a2a_bytes,
+                       "note": "4 all-to-alls (q, k, v, o) per layer; NVLink 900 GB/s/dir nominal"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -74,6 +74,67 @@ typedef struct vx_attn_args {
 
 int vx_attn_fwd(const vx_attn_args* args, vx_stream_t stream);
 
+/* ----------------------------------------------------------------------
+ * DeepSpeed-Ulysses head-slab packing (one batch item per call).
+ *
+ * Replaces the layout half of the tiled jax.lax.all_to_all calls in
+ * sequence_parallel_self_attention (src/vidax/core/attention.py:379-381 and
+ * :388): after vx_ulysses_pack, chunk g of `dst` (groups equal contiguous
+ * chunks) holds head group g of every local token, so one equal-split
+ * all-to-all (NCCL) delivers the tokens->heads reshard; the receiver's buffer
+ * (groups_src, seq, hg, D) is the full sequence in source-rank order.
+ * hg = ceil(heads / groups); pack writes zeros for heads >= `heads`
+ * (head padding when heads % groups != 0) and unpack drops them.
+ */
+typedef struct vx_head_slab_args {
+  int32_t num_tensors;   /* 1..3 (e.g. q, k, v in one launch) */
+  const void* src[3];
+  void* dst[3];
+  int64_t stride[3][2];  /* strided side, element strides of (seq, heads); d stride 1 */
+  int32_t seq, heads, head_dim, groups;
+} vx_head_slab_args;
+
+/* strided (seq, heads, D) rows -> contiguous (groups, seq, hg, D) */
+int vx_ulysses_pack(const vx_head_slab_args* args, vx_stream_t stream);
+/* contiguous (groups, seq, hg, D) -> strided (seq, heads, D) rows */
+int vx_ulysses_unpack(const vx_head_slab_args* args, vx_stream_t stream);
+
+/* ----------------------------------------------------------------------
+ * 3-D neighborhood attention (NATTEN-style clamped windows, non-causal).
+ *
+ * Replaces vidax.models.ltx2_5.diffusion_vae.neighborhood_attention_3d
+ * (src/vidax/models/ltx2_5/diffusion_vae.py:179-234): for query (t, h, w)
+ * the keys are [st(t), st(t)+Kt) x [st(h), st(h)+Kh) x [st(w), st(w)+Kw) with
+ * K = min(kernel, L) and st(i) = clamp(i - K/2, 0, L - K) (_window_start,
+ * :152-164); softmax in fp32 over those keys. vidax pre-scales q by the
+ * caller (:265), so `scale` is normally 1. With round_logits = 1 the q.k
+ * products are rounded to bf16 before the softmax, as the reference's bf16
+ * einsum does (:222).
+ */
+typedef struct vx_na3d_args {
+  const void* q;  /* (B, T, H, W, NH, HD) bf16 */
+  const void* k;  /* (B, T, H, W, NHkv, HD) bf16 */
+  const void* v;
+  void* o;        /* (B, T, H, W, NH, HD) bf16 */
+  int64_t q_stride[5]; /* element strides of (b, t, h, w, head); d stride 1; b stride = T * t stride */
+  int64_t k_stride[5];
+  int64_t v_stride[5];
+  int64_t o_stride[5];
+  int32_t batch, T, H, W, heads, heads_kv, head_dim;
+  int32_t kernel_t, kernel_h, kernel_w;
+  float scale;
+  int32_t round_logits;
+  int32_t q_box[3];    /* query tile box (t, h, w), product 128; all 0 = choose automatically */
+  int32_t pair_axis;   /* axis along which a CTA pairs two query boxes; ignored when q_box is 0 */
+} vx_na3d_args;
+
+int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);
+
+/* Host helper: start_out[i] = clamp(i - K/2, 0, length - K), K = min(kernel,
+ * length), i in [0, length) -- the window-start contract of _window_start
+ * (diffusion_vae.py:152-164). Returns VX_EINVAL for length/kernel < 1. */
+int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,51 @@
+"""Worker for test_ulysses_two_gpus_nccl (run under torch.distributed.run):
+each rank feeds its chunk_by_rank share of a seeded global sequence through
+sequence_parallel_self_attention over NCCL; rank 0 gathers and compares with
+the oracle."""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import vidax_b200 as vx  # noqa: E402
+from oracle.attention_ref import compare, sdpa, seeded_qkv  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    vx.register_axis("sp", None)
+    ok = True
+    for (B, S, H) in [(1, 1024, 8), (2, 768, 6), (1, 512, 3)]:
+        q, k, v = seeded_qkv((B, S, H, 128), 900 + S + H)
+        sl = S // world
+        mine = [torch.from_numpy(np.ascontiguousarray(x[:, rank * sl:(rank + 1) * sl])).cuda().bfloat16()
+                for x in (q, k, v)]
+        out = vx.sequence_parallel_self_attention(*mine, "sp")
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out.contiguous())
+        if rank == 0:
+            got = torch.cat(gathered, dim=1).float().cpu().numpy()
+            mx, mean = compare(got, sdpa(q, k, v))
+            print(f"B={B} S={S} H={H}: max {mx:.3g} mean {mean:.3g}", flush=True)
+            ok = ok and mx <= 2e-2 and mean <= 2e-3
+    flag = torch.tensor([1 if ok else 0], device="cuda")
+    dist.broadcast(flag, 0)
+    vx.unregister_axis("sp")
+    dist.destroy_process_group()
+    if rank == 0:
+        print("ULYSSES OK" if flag.item() else "ULYSSES FAIL", flush=True)
+    sys.exit(0 if flag.item() else 1)
+
+
+if __name__ == "__main__":
+    main()

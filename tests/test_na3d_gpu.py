@@ -1,0 +1,135 @@
+"""GPU parity of the sm_100a 3-D neighborhood-attention kernel.
+
+Window/mask indexing is checked bit-exactly through a one-hot probe (values
+that identify each key), outputs against the CPU oracle within max-abs 2e-2
+and mean-abs 2e-3 of the fp32-softmax reference.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention_ref import compare, seeded_qkv, to_bf16
+from oracle.na3d_ref import na3d, window_sets
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+
+
+def _dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).to("cuda").to(torch.bfloat16)
+
+
+def _status_clean():
+    from vidax_b200 import _lib
+    return _lib.device_status(clear=True) == 0
+
+
+CASES = [
+    # (B, T, H, W, NH), kernel
+    ((1, 3, 5, 7, 2), (3, 3, 5)),
+    ((1, 4, 9, 17, 1), (3, 5, 5)),
+    ((2, 5, 6, 11, 2), (3, 7, 7)),
+    ((1, 2, 3, 4, 1), (5, 9, 9)),       # kernel larger than the grid on every axis
+    ((1, 6, 10, 40, 1), (5, 9, 9)),
+    ((1, 3, 20, 33, 3), (1, 1, 1)),     # degenerate window: output == v
+    ((1, 12, 12, 12, 1), (11, 11, 11)),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,kernel", CASES)
+def test_na3d_matches_oracle(shape, kernel):
+    import vidax_b200 as vx
+    B, T, H, W, NH = shape
+    q, k, v = seeded_qkv((B, T, H, W, NH, 128), 500 + T * 7 + W, n=3)
+    q = to_bf16(q * np.float32(128 ** -0.5))
+    out = vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), kernel)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    ref = na3d(q, k, v, kernel)
+    mx, mean = compare(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("q_box,pair", [((2, 8, 8), 0), ((1, 8, 16), 2), ((4, 4, 8), 1),
+                                        ((1, 2, 64), 0), ((8, 4, 4), 2)])
+def test_na3d_every_tiling_agrees(q_box, pair):
+    """Every query tiling gives the oracle's result (tiling is a schedule choice only)."""
+    import vidax_b200 as vx
+    B, T, H, W, NH = 1, 7, 13, 21, 2
+    q, k, v = seeded_qkv((B, T, H, W, NH, 128), 77, n=3)
+    q = to_bf16(q * np.float32(128 ** -0.5))
+    out = vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (5, 9, 9),
+                                       q_box=q_box, pair_axis=pair)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    mx, mean = compare(out.float().cpu().numpy(), na3d(q, k, v, (5, 9, 9)))
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
+def test_na3d_window_sets_bit_exact():
+    """Attended key sets are exactly the reference windows: with q = 0 every
+    visible key gets equal weight, so v = one-hot(key index bits) makes the
+    output the mean of the attended keys' codes; with |window| a power of two
+    this mean is exact in bf16 only if the set is exactly right. Instead of
+    relying on rounding, each key's code is a distinct small integer and the
+    output sum * |window| must equal the exact code sum per query."""
+    import vidax_b200 as vx
+    B, T, H, W, NH = 1, 5, 7, 11, 1
+    kernel = (3, 5, 3)
+    q = np.zeros((B, T, H, W, NH, 128), np.float32)
+    k = np.zeros_like(q)
+    # v[..., c] = bit c of the key's linear index (keys 0..384 need 9 bits)
+    v = np.zeros_like(q)
+    lin = np.arange(T * H * W).reshape(T, H, W)
+    for c in range(9):
+        v[0, :, :, :, 0, c] = (lin >> c) & 1
+    out = vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), kernel).float().cpu().numpy()
+    torch.cuda.synchronize()
+    (st_t, kt), (st_h, kh), (st_w, kw) = window_sets(T, H, W, kernel)
+    n = kt * kh * kw
+    for t in range(T):
+        for h in range(H):
+            for w in range(W):
+                keys = lin[st_t[t]:st_t[t] + kt, st_h[h]:st_h[h] + kh, st_w[w]:st_w[w] + kw].ravel()
+                expect = np.array([((keys >> c) & 1).sum() for c in range(9)], np.float64) / n
+                got = out[0, t, h, w, 0, :9]
+                # each channel is a count/n in [0, 1]; bf16 keeps 8 bits, so
+                # compare the recovered counts
+                assert np.array_equal(np.rint(got * n), np.rint(expect * n)), (t, h, w)
+
+
+@pytest.mark.gpu
+def test_na3d_round_logits_matches_reference_rounding():
+    import vidax_b200 as vx
+    B, T, H, W, NH = 1, 4, 6, 10, 2
+    q, k, v = seeded_qkv((B, T, H, W, NH, 128), 91, n=3)
+    q = to_bf16(q * np.float32(128 ** -0.5))
+    out = vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (3, 5, 5), round_logits=True)
+    torch.cuda.synchronize()
+    ref = na3d(q, k, v, (3, 5, 5), round_logits=True)
+    mx, mean = compare(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
+def test_cfg4_sampled_positions():
+    """(1, 21, 30, 52, 24, 128), window 5x9x9, q pre-scaled;
+    a seeded sample of query positions (all faces and corners included)."""
+    import vidax_b200 as vx
+    shape = (1, 21, 30, 52, 24, 128)
+    q, k, v = seeded_qkv(shape, 4, n=3)
+    q = to_bf16(q * np.float32(128 ** -0.5))
+    out = vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (5, 9, 9))
+    torch.cuda.synchronize()
+    assert _status_clean()
+    rng = np.random.default_rng(4)
+    pos = np.stack([rng.integers(0, 21, 40), rng.integers(0, 30, 40), rng.integers(0, 52, 40)], 1)
+    corners = np.array([[t, h, w] for t in (0, 20) for h in (0, 29) for w in (0, 51)])
+    pos = np.concatenate([pos, corners, [[10, 15, 26], [1, 1, 1], [19, 28, 50]]])
+    ref = na3d(q, k, v, (5, 9, 9), positions=pos)
+    got = out.float().cpu().numpy()[0][pos[:, 0], pos[:, 1], pos[:, 2]][None]
+    mx, mean = compare(got, ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

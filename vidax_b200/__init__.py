@@ -4,7 +4,12 @@ Public API (same names and arguments as vidax.core.attention and
 vidax.models.ltx2_5.diffusion_vae.neighborhood_attention_3d, on torch CUDA
 tensors):
 
-    dot_product_attention, local_attention, chunk_by_rank
+    dot_product_attention, local_attention, chunk_by_rank,
+    sequence_parallel_self_attention, sequence_parallel_joint_self_attention,
+    neighborhood_attention_3d
+
+Mesh axes (vidax's `sp` axis inside shard_map) bind to torch.distributed
+process groups with `register_axis(name, group)`.
 """
 from .attention import (  # noqa: F401
     attention_flops,
@@ -12,6 +17,15 @@ from .attention import (  # noqa: F401
     dot_product_attention,
     flash_attention,
     local_attention,
+)
+from .neighborhood import na3d_flops, neighborhood_attention_3d  # noqa: F401
+from .ulysses import (  # noqa: F401
+    axis_index,
+    axis_size,
+    register_axis,
+    sequence_parallel_joint_self_attention,
+    sequence_parallel_self_attention,
+    unregister_axis,
 )
 
 __version__ = "0.1.0"

@@ -191,22 +191,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
+    // Per KV tile j (all loaded in order): release K(j) (its S MMAs were
+    // issued earlier), then for each query tile t that needs j:
+    //   PV_t(j) after P_t(j) is ready, then S_t(j+1) if t needs j+1.
+    // A query tile that does not need a KV tile skips it entirely (the
+    // neighborhood geometry; the dense one needs every tile).
     if (lane == 0 && n_kv > 0) {
-      const uint32_t q0 = sbase + kSmemQ, q1 = sbase + kSmemQ + kTileBytes;
-      const uint32_t t_s0 = tmem, t_s1 = tmem + 128, t_o0 = tmem + 256, t_o1 = tmem + 384;
+      const uint32_t q_sm[2] = {sbase + kSmemQ, sbase + kSmemQ + kTileBytes};
       bool ok = mbar_wait(bar(kQFull + 0), 0, abort_flag, status, kDevTimeoutMma) &&
+                mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma) &&
                 mbar_wait(bar(kKFull + 0), 0, abort_flag, status, kDevTimeoutMma);
+      int last[2] = {geo.last_tile(0), geo.last_tile(1)};
+      int pv_count[2] = {0, 0};
       if (ok) {
         tc_fence_after();
-        issue_qk(t_s0, q0, sbase + kSmemK);
-        tc_commit(bar(kSFull + 0));
-      }
-      ok = ok && mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(t_s1, q1, sbase + kSmemK);
-        tc_commit(bar(kSFull + 1));
-        tc_commit(bar(kKEmpty + 0));
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (geo.needs(t, 0)) {
+            issue_qk(tmem + 128 * t, q_sm[t], sbase + kSmemK);
+            tc_commit(bar(kSFull + t));
+          }
+        }
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % kStages;
@@ -216,27 +221,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool has_next = j + 1 < n_kv;
         const uint32_t v_sm = sbase + kSmemV + s * kTileBytes;
         const uint32_t k_next = sbase + kSmemK + s1 * kTileBytes;
+        tc_commit(bar(kKEmpty + s));  // every S(j) MMA was issued before this point
         if (!mbar_wait(bar(kVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
-        if (!mbar_wait(bar(kPFull + 0), j & 1, abort_flag, status, kDevTimeoutMma)) break;
-        tc_fence_after();
-        issue_pv(t_o0, t_s0, v_sm, j > 0);
-        if (!has_next) tc_commit(bar(kOFull + 0));
-        if (has_next) {
-          if (!mbar_wait(bar(kKFull + s1), ph1, abort_flag, status, kDevTimeoutMma)) break;
-          tc_fence_after();
-          issue_qk(t_s0, q0, k_next);
-          tc_commit(bar(kSFull + 0));
+        bool k_next_ready = false;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (geo.needs(t, j)) {
+            if (!mbar_wait(bar(kPFull + t), pv_count[t] & 1, abort_flag, status, kDevTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(tmem + 256 + 128 * t, tmem + 128 * t, v_sm, pv_count[t] > 0);
+            ++pv_count[t];
+            if (j == last[t]) tc_commit(bar(kOFull + t));
+          }
+          if (has_next && geo.needs(t, j + 1)) {
+            if (!k_next_ready) {
+              if (!mbar_wait(bar(kKFull + s1), ph1, abort_flag, status, kDevTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next_ready = true;
+            }
+            issue_qk(tmem + 128 * t, q_sm[t], k_next);
+            tc_commit(bar(kSFull + t));
+          }
         }
-        if (!mbar_wait(bar(kPFull + 1), j & 1, abort_flag, status, kDevTimeoutMma)) break;
-        tc_fence_after();
-        issue_pv(t_o1, t_s1, v_sm, j > 0);
+        if (!ok) break;
         tc_commit(bar(kVEmpty + s));
-        if (!has_next) tc_commit(bar(kOFull + 1));
-        if (has_next) {
-          issue_qk(t_s1, q1, k_next);
-          tc_commit(bar(kSFull + 1));
-          tc_commit(bar(kKEmpty + s1));
-        }
       }
       // Drain: no MMA may still be running when TMEM is released.
       tc_commit(bar(kDrain));
@@ -257,8 +271,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_used = neg_inf();
     float l_sum = 0.f;
     bool ok = true;
+    int count = 0;  // KV tiles this query tile has processed
     for (int j = 0; j < n_kv; ++j) {
-      ok = mbar_wait(bar(kSFull + wg), j & 1, abort_flag, status, kDevTimeoutSoftmax);
+      if (!geo.needs(wg, j)) continue;
+      ok = mbar_wait(bar(kSFull + wg), count & 1, abort_flag, status, kDevTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -287,9 +303,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need = m_new > m_used + kRescaleThreshold;
       float alpha = 1.f;
       if (need) alpha = ex2_approx(m_used - m_new);  // 0 when m_used = -inf
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O(j-1) is complete: S(j) was issued after PV(j-1) and its commit
-        // tracks every earlier MMA. Rescale this warp's 32 rows of O.
+      if (count > 0 && __any_sync(0xffffffffu, need)) {
+        // O is complete up to this query tile's previous KV tile: S(j) was
+        // issued after that PV and its commit tracks every earlier MMA.
+        // Rescale this warp's 32 rows of O.
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t orr[32];
@@ -323,9 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kPFull + wg));
+      ++count;
     }
 
-    if (n_kv == 0) {
+    if (ok && count == 0) {
       geo.store_zero_row(wg, row);
     } else if (ok) {
       ok = mbar_wait(bar(kOFull + wg), 0, abort_flag, status, kDevTimeoutSoftmax);
@@ -391,6 +409,8 @@ struct DenseGeo {
     kv_valid = kv;
   }
   __device__ int num_kv_tiles() const { return (kv_valid + kBlockN - 1) / kBlockN; }
+  __device__ bool needs(int, int) const { return true; }
+  __device__ int last_tile(int) const { return num_kv_tiles() - 1; }
   __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
                          uint64_t pol) const {
     tma_load_4d(dst, tm, bar, 0, h, q0 + t * kBlockM, b, pol);
@@ -434,6 +454,222 @@ struct DenseGeo {
     if (p.lse == nullptr || row_global >= p.Sq) return;
     p.lse[(static_cast<long long>(b) * p.H + h) * p.Sq + row_global] = lse;
   }
+};
+
+}  // namespace attn
+}  // namespace vx
+
+namespace vx {
+namespace attn {
+
+// --------------------------------------------------------------------------
+// 3-D neighborhood geometry (vidax.models.ltx2_5.diffusion_vae
+// .neighborhood_attention_3d, src/vidax/models/ltx2_5/diffusion_vae.py:152-234).
+//
+// Query (t, h, w) attends the keys in the clamped window
+//   [st(t), st(t)+Kt) x [st(h), st(h)+Kh) x [st(w), st(w)+Kw),
+//   st(i) = clamp(i - K/2, 0, L - K),  K = min(kernel, L)
+// (_window_start, diffusion_vae.py:152-164). Tensors are (B, T, H, W, NH, HD);
+// the tensor maps are 5-D {HD, NH, W, H, B*T} (batch and time merged).
+//
+// A query tile is a box of qt x qh x qw = 128 queries (row order w fastest,
+// then h, then t, as TMA writes it); a CTA owns two boxes adjacent along
+// `pair_axis`. The CTA visits the key tiles (boxes of KT x KH x KW = 128 keys)
+// that tile the union of both boxes' windows; each query tile processes only
+// the key tiles that meet its own window union, and masks keys outside each
+// query's window. Every window is non-empty, so every valid query sees >= 1
+// key.
+struct NaParams {
+  __nv_bfloat16* o;
+  long long o_sb, o_st, o_sh, o_sw, o_shead;  // output strides in elements
+  int* status;
+  int B, T, H, W, NH, NHkv;
+  int kt, kh, kw;          // effective window (kernel clamped to the grid)
+  int qbox[3];             // query box (t, h, w), product 128
+  int pair_axis;           // 0 = t, 1 = h, 2 = w
+  int regions[3];          // CTA regions per axis
+  float scale_log2;
+  int round_logits;        // round q.k to bf16 before the softmax (vidax's einsum output dtype)
+};
+
+__device__ __forceinline__ int na_start(int i, int L, int k) {
+  return min(max(i - k / 2, 0), L - k);
+}
+
+// bits [lo, hi) of an n-bit field (0 <= lo, hi clamped to [0, n])
+__device__ __forceinline__ uint32_t bit_range(int lo, int hi, int n) {
+  lo = max(lo, 0);
+  hi = min(hi, n);
+  if (hi <= lo) return 0u;
+  const uint32_t upto_hi = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+  const uint32_t upto_lo = (1u << lo) - 1u;
+  return upto_hi & ~upto_lo;
+}
+
+template <int KT, int KH, int KW>
+struct NaGeo {
+  static_assert(KT * KH * KW == 128, "key tile must hold 128 keys");
+  static_assert(KW == 8 || KW == 16 || KW == 32, "key tile width 8, 16 or 32");
+  using Params = NaParams;
+  const NaParams& p;
+  int b, head, head_kv;
+  int org[2][3];          // query tile origins
+  int lim[3];             // grid extents (T, H, W)
+  int u0[3], n_ax[3];     // CTA key union start and tiles per axis
+  int wu0[2][3], wu1[2][3];  // per query tile key union [wu0, wu1)
+  int n_tiles;
+  // softmax row state
+  int qc[3];              // query coordinates of this thread's row
+  int ws[3];              // window starts
+  bool row_valid;
+
+  __device__ NaGeo(const NaParams& prm, int*) : p(prm) {
+    head = blockIdx.y;
+    b = blockIdx.z;
+    head_kv = head / (p.NH / p.NHkv);
+    lim[0] = p.T;
+    lim[1] = p.H;
+    lim[2] = p.W;
+    const int ksz[3] = {p.kt, p.kh, p.kw};
+    int reg[3];
+    int r = blockIdx.x;
+    reg[2] = r % p.regions[2];
+    r /= p.regions[2];
+    reg[1] = r % p.regions[1];
+    reg[0] = r / p.regions[1];
+    const int kvb[3] = {KT, KH, KW};
+    int cu0[3] = {0, 0, 0}, cu1[3] = {0, 0, 0};
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      const int rsz = p.qbox[a] * (a == p.pair_axis ? 2 : 1);
+      const int r0 = reg[a] * rsz;
+      org[0][a] = r0;
+      org[1][a] = r0 + (a == p.pair_axis ? p.qbox[a] : 0);
+      bool first = true;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int a0 = org[t][a];
+        const int a1 = min(a0 + p.qbox[a], lim[a]);
+        if (a0 < a1) {
+          wu0[t][a] = na_start(a0, lim[a], ksz[a]);
+          wu1[t][a] = na_start(a1 - 1, lim[a], ksz[a]) + ksz[a];
+          if (first) {
+            cu0[a] = wu0[t][a];
+            cu1[a] = wu1[t][a];
+            first = false;
+          } else {
+            cu0[a] = min(cu0[a], wu0[t][a]);
+            cu1[a] = max(cu1[a], wu1[t][a]);
+          }
+        } else {
+          wu0[t][a] = 0;
+          wu1[t][a] = 0;  // empty: this query tile lies outside the grid
+        }
+      }
+      u0[a] = cu0[a];
+      n_ax[a] = cu1[a] > cu0[a] ? (cu1[a] - cu0[a] + kvb[a] - 1) / kvb[a] : 0;
+    }
+    n_tiles = n_ax[0] * n_ax[1] * n_ax[2];
+  }
+
+  __device__ int num_kv_tiles() const { return n_tiles; }
+  __device__ void tile_origin(int j, int (&o)[3]) const {
+    const int jw = j % n_ax[2];
+    const int r = j / n_ax[2];
+    const int jh = r % n_ax[1];
+    const int jt = r / n_ax[1];
+    o[0] = u0[0] + jt * KT;
+    o[1] = u0[1] + jh * KH;
+    o[2] = u0[2] + jw * KW;
+  }
+  __device__ bool needs(int t, int j) const {
+    int o[3];
+    tile_origin(j, o);
+    const int kvb[3] = {KT, KH, KW};
+    bool hit = true;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) hit = hit && (o[a] < wu1[t][a]) && (wu0[t][a] < o[a] + kvb[a]);
+    return hit;
+  }
+  __device__ int last_tile(int t) const {
+    for (int j = n_tiles - 1; j >= 0; --j)
+      if (needs(t, j)) return j;
+    return -1;
+  }
+  __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
+                         uint64_t pol) const {
+    const int bt = b * p.T + org[t][0];
+    tma_load_5d(dst, tm, bar, 0, head, org[t][2], org[t][1], bt, pol);
+    tma_load_5d(dst + kHalfBytes, tm, bar, 64, head, org[t][2], org[t][1], bt, pol);
+  }
+  __device__ void load_kv(const CUtensorMap* tm, int j, uint32_t dst, uint32_t bar,
+                          uint64_t pol) const {
+    int o[3];
+    tile_origin(j, o);
+    const int bt = b * p.T + o[0];
+    tma_load_5d(dst, tm, bar, 0, head_kv, o[2], o[1], bt, pol);
+    tma_load_5d(dst + kHalfBytes, tm, bar, 64, head_kv, o[2], o[1], bt, pol);
+  }
+  __device__ void softmax_setup(int t, int row) {
+    const int qw = p.qbox[2], qh = p.qbox[1];
+    const int iw = row % qw;
+    const int ih = (row / qw) % qh;
+    const int it = row / (qw * qh);
+    qc[0] = org[t][0] + it;
+    qc[1] = org[t][1] + ih;
+    qc[2] = org[t][2] + iw;
+    row_valid = qc[0] < p.T && qc[1] < p.H && qc[2] < p.W;
+    const int ksz[3] = {p.kt, p.kh, p.kw};
+#pragma unroll
+    for (int a = 0; a < 3; ++a) ws[a] = na_start(min(qc[a], lim[a] - 1), lim[a], ksz[a]);
+  }
+  // Column c of a key tile is key (ct, ch, cw) = (c / (KH*KW), (c / KW) % KH,
+  // c % KW) of the tile box; it is visible when each coordinate lies in this
+  // row's window. Masks are built per axis as bit fields, then per 32-column
+  // chunk.
+  __device__ void mask_scores(int j, uint32_t (&sr)[4][32]) const {
+    int o[3];
+    tile_origin(j, o);
+    const uint32_t tmask = bit_range(ws[0] - o[0], ws[0] + p.kt - o[0], KT);
+    const uint32_t hmask = bit_range(ws[1] - o[1], ws[1] + p.kh - o[1], KH);
+    const uint32_t wmask = bit_range(ws[2] - o[2], ws[2] + p.kw - o[2], KW);
+    constexpr int kRowsPerChunk = 32 / KW;  // (ct, ch) rows of the tile per chunk (>= 1)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t m = 0;
+#pragma unroll
+      for (int rr = 0; rr < kRowsPerChunk; ++rr) {
+        const int tile_row = c * kRowsPerChunk + rr;  // = ct * KH + ch
+        const int ct = tile_row / KH, ch = tile_row % KH;
+        const bool on = ((tmask >> ct) & 1u) && ((hmask >> ch) & 1u);
+        if (on) m |= (KW == 32 ? wmask : (wmask << (rr * KW)));
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float x = __uint_as_float(sr[c][i]);
+        if (p.round_logits) x = __bfloat162float(__float2bfloat16_rn(x));
+        sr[c][i] = ((m >> i) & 1u) ? __float_as_uint(x) : 0xff800000u;
+      }
+    }
+  }
+  __device__ __nv_bfloat16* row_ptr() const {
+    return p.o + b * p.o_sb + qc[0] * p.o_st + qc[1] * p.o_sh + qc[2] * p.o_sw +
+           head * p.o_shead;
+  }
+  __device__ void store_row_chunk(int, int, int c, const uint32_t (&pk)[16]) const {
+    if (!row_valid) return;
+    uint4* dst = reinterpret_cast<uint4*>(row_ptr() + c * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+  }
+  __device__ void store_zero_row(int, int) const {
+    if (!row_valid) return;
+    uint4* dst = reinterpret_cast<uint4*>(row_ptr());
+#pragma unroll
+    for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+  }
+  __device__ void store_lse(int, int, float) const {}
 };
 
 }  // namespace attn

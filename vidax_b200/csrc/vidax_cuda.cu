@@ -8,14 +8,18 @@
 
 #include <cstdarg>
 #include <cstdio>
-#include <cstring>
+#include <algorithm>
+#include <array>
 #include <cmath>
+#include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
 #include <string>
 #include <utility>
 
 #include "attn_sm100.cuh"
+#include "ulysses_pack.cuh"
 
 namespace {
 
@@ -231,6 +235,269 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
   kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
+  return VX_OK;
+}
+
+
+static int head_slab(const vx_head_slab_args* a, vx_stream_t stream, bool pack) {
+  using namespace vx::ulysses;
+  if (a == nullptr) return fail(VX_EINVAL, "args is NULL");
+  if (a->num_tensors < 1 || a->num_tensors > 3)
+    return fail(VX_EINVAL, "num_tensors must be 1..3 (got %d)", a->num_tensors);
+  if (a->seq < 0 || a->heads <= 0 || a->groups <= 0)
+    return fail(VX_EINVAL, "bad sizes (seq=%d heads=%d groups=%d)", a->seq, a->heads, a->groups);
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return fail(VX_EUNSUPPORTED, "head_dim %d (64, 128 or 256)", a->head_dim);
+  if (a->groups > 65535) return fail(VX_EUNSUPPORTED, "groups must be <= 65535");
+  if (a->seq == 0) return VX_OK;
+  PackParams p;
+  const int vpd = a->head_dim / 8;
+  p.vpd_log2 = vpd == 8 ? 3 : (vpd == 16 ? 4 : 5);
+  p.num_tensors = a->num_tensors;
+  p.seq = a->seq;
+  p.heads = a->heads;
+  p.groups = a->groups;
+  p.hg = (a->heads + a->groups - 1) / a->groups;
+  for (int t = 0; t < 3; ++t) {
+    p.src[t] = nullptr;
+    p.dst[t] = nullptr;
+    p.s_stride[t] = p.h_stride[t] = 0;
+  }
+  for (int t = 0; t < a->num_tensors; ++t) {
+    if (a->src[t] == nullptr || a->dst[t] == nullptr)
+      return fail(VX_EINVAL, "tensor %d: NULL pointer", t);
+    if (!aligned16(a->src[t]) || !aligned16(a->dst[t]))
+      return fail(VX_EINVAL, "tensor %d: pointers must be 16-byte aligned", t);
+    if (a->stride[t][0] % 8 != 0 || a->stride[t][1] % 8 != 0 || a->stride[t][0] < 0 ||
+        a->stride[t][1] < 0)
+      return fail(VX_EINVAL, "tensor %d: strides must be non-negative multiples of 8 elements", t);
+    p.src[t] = static_cast<const uint4*>(a->src[t]);
+    p.dst[t] = static_cast<uint4*>(a->dst[t]);
+    p.s_stride[t] = a->stride[t][0] / 8;
+    p.h_stride[t] = a->stride[t][1] / 8;
+  }
+  const long long plane = static_cast<long long>(a->seq) * (p.hg << p.vpd_log2);
+  long long bx = (plane + 255) / 256;
+  if (bx > 4096) bx = 4096;
+  dim3 grid(static_cast<unsigned>(bx), a->groups, a->num_tensors);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pack)
+    head_slab_kernel<true><<<grid, 256, 0, st>>>(p);
+  else
+    head_slab_kernel<false><<<grid, 256, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, pack ? "ulysses pack launch" : "ulysses unpack launch");
+  return VX_OK;
+}
+
+int vx_ulysses_pack(const vx_head_slab_args* a, vx_stream_t stream) { return head_slab(a, stream, true); }
+int vx_ulysses_unpack(const vx_head_slab_args* a, vx_stream_t stream) {
+  return head_slab(a, stream, false);
+}
+
+}  // extern "C"
+
+namespace {
+
+constexpr int kNaKT = 2, kNaKH = 4, kNaKW = 16;
+using NaGeoDefault = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW>;
+
+int na_start_host(int i, int L, int k) { return std::min(std::max(i - k / 2, 0), L - k); }
+
+// MMA work (key tiles processed summed over query tiles) of one tiling on a
+// T x H x W grid with effective window (kt, kh, kw); mirrors NaGeo exactly.
+long long na_tiling_cost(const int lim[3], const int ksz[3], const int qbox[3], int pair) {
+  const int kvb[3] = {kNaKT, kNaKH, kNaKW};
+  int rsz[3], regions[3];
+  for (int a = 0; a < 3; ++a) {
+    rsz[a] = qbox[a] * (a == pair ? 2 : 1);
+    regions[a] = (lim[a] + rsz[a] - 1) / rsz[a];
+  }
+  long long cost = 0;
+  for (int rt = 0; rt < regions[0]; ++rt)
+    for (int rh = 0; rh < regions[1]; ++rh)
+      for (int rw = 0; rw < regions[2]; ++rw) {
+        const int reg[3] = {rt, rh, rw};
+        int wu0[2][3], wu1[2][3], cu0[3], cu1[3];
+        for (int a = 0; a < 3; ++a) {
+          bool first = true;
+          for (int t = 0; t < 2; ++t) {
+            const int a0 = reg[a] * rsz[a] + (t == 1 && a == pair ? qbox[a] : 0);
+            const int a1 = std::min(a0 + qbox[a], lim[a]);
+            if (a0 < a1) {
+              wu0[t][a] = na_start_host(a0, lim[a], ksz[a]);
+              wu1[t][a] = na_start_host(a1 - 1, lim[a], ksz[a]) + ksz[a];
+              if (first) { cu0[a] = wu0[t][a]; cu1[a] = wu1[t][a]; first = false; }
+              else { cu0[a] = std::min(cu0[a], wu0[t][a]); cu1[a] = std::max(cu1[a], wu1[t][a]); }
+            } else {
+              wu0[t][a] = wu1[t][a] = 0;
+            }
+          }
+          if (first) { cu0[a] = cu1[a] = 0; }
+        }
+        for (int t = 0; t < 2; ++t) {
+          long long tiles = 1;
+          for (int a = 0; a < 3; ++a) {
+            // key tiles of the CTA grid (aligned at cu0) that meet [wu0, wu1)
+            if (wu1[t][a] <= wu0[t][a]) { tiles = 0; break; }
+            const int first_tile = (wu0[t][a] - cu0[a]) / kvb[a];
+            const int last_tile = (wu1[t][a] - 1 - cu0[a]) / kvb[a];
+            tiles *= (last_tile - first_tile + 1);
+          }
+          cost += tiles;
+        }
+      }
+  return cost;
+}
+
+struct NaChoice { int qbox[3]; int pair; };
+
+NaChoice na_choose_tiling(const int lim[3], const int ksz[3]) {
+  static std::mutex mu;
+  static std::map<std::array<int, 6>, NaChoice> cache;
+  const std::array<int, 6> key = {lim[0], lim[1], lim[2], ksz[0], ksz[1], ksz[2]};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  static const int cands[][3] = {{2, 8, 8}, {1, 8, 16}, {4, 4, 8}, {2, 4, 16}, {1, 16, 8},
+                                 {4, 8, 4}, {8, 4, 4},  {1, 4, 32}, {2, 16, 4}, {1, 2, 64},
+                                 {8, 2, 8}, {4, 2, 16}, {1, 32, 4}, {16, 2, 4}, {2, 2, 32}};
+  NaChoice best = {{2, 8, 8}, 0};
+  long long best_cost = -1;
+  for (const auto& c : cands)
+    for (int pair = 0; pair < 3; ++pair) {
+      const long long cost = na_tiling_cost(lim, ksz, c, pair);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best = {{c[0], c[1], c[2]}, pair};
+      }
+    }
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = best;
+  return best;
+}
+
+bool is_pow2(int x) { return x > 0 && (x & (x - 1)) == 0; }
+
+// (B, T, H, W, NH, HD) operand -> 5-D map {HD, NH, W, H, B*T}.
+int na_tmap(CUtensorMap* tm, const char* name, const void* ptr, const int64_t* st, int B, int T,
+            int H, int W, int NH, int HD, const int box_thw[3]) {
+  if (ptr == nullptr) return fail(VX_EINVAL, "%s is NULL", name);
+  if (!aligned16(ptr)) return fail(VX_EINVAL, "%s must be 16-byte aligned", name);
+  for (int i = 0; i < 5; ++i)
+    if (st[i] <= 0 || st[i] % 8 != 0)
+      return fail(VX_EINVAL, "%s stride[%d]=%lld must be a positive multiple of 8 elements", name,
+                  i, (long long)st[i]);
+  if (B > 1 && st[0] != static_cast<int64_t>(T) * st[1])
+    return fail(VX_EINVAL, "%s: batch stride must equal T * time stride (merged B*T axis)", name);
+  const uint64_t dims[5] = {(uint64_t)HD, (uint64_t)NH, (uint64_t)W, (uint64_t)H,
+                            (uint64_t)B * (uint64_t)T};
+  const uint64_t strides[4] = {(uint64_t)st[4] * 2, (uint64_t)st[3] * 2, (uint64_t)st[2] * 2,
+                               (uint64_t)st[1] * 2};
+  const uint32_t box[5] = {64, 1, (uint32_t)box_thw[2], (uint32_t)box_thw[1], (uint32_t)box_thw[0]};
+  return make_tmap(tm, ptr, 5, dims, strides, box);
+}
+
+}  // namespace
+
+extern "C" {
+
+int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out) {
+  if (length < 1 || kernel < 1) return fail(VX_EINVAL, "length and kernel must be >= 1");
+  if (start_out == nullptr) return fail(VX_EINVAL, "start_out is NULL");
+  const int k = std::min(kernel, length);
+  for (int i = 0; i < length; ++i) start_out[i] = na_start_host(i, length, k);
+  return VX_OK;
+}
+
+int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
+  using namespace vx::attn;
+  if (a == nullptr) return fail(VX_EINVAL, "args is NULL");
+  if (a->batch < 0 || a->T < 0 || a->H < 0 || a->W < 0 || a->heads <= 0 || a->heads_kv <= 0)
+    return fail(VX_EINVAL, "bad sizes");
+  if (a->heads % a->heads_kv != 0) return fail(VX_EINVAL, "heads must be a multiple of heads_kv");
+  if (a->kernel_t < 1 || a->kernel_h < 1 || a->kernel_w < 1)
+    return fail(VX_EINVAL, "kernel sizes must be >= 1");
+  if (a->head_dim != kHeadDim)
+    return fail(VX_EUNSUPPORTED, "head_dim %d (this build implements %d)", a->head_dim, kHeadDim);
+  if (!(a->scale > 0.f) || !std::isfinite(a->scale))
+    return fail(VX_EUNSUPPORTED, "scale must be finite and > 0");
+  if (a->batch == 0 || a->T == 0 || a->H == 0 || a->W == 0) return VX_OK;
+  if ((long long)a->batch * a->T > (1LL << 31) - 1) return fail(VX_EUNSUPPORTED, "B*T too large");
+  if (a->heads > 65535 || a->batch > 65535) return fail(VX_EUNSUPPORTED, "heads/batch > 65535");
+  if (a->o == nullptr || !aligned16(a->o)) return fail(VX_EINVAL, "o must be non-NULL and 16-byte aligned");
+  for (int i = 0; i < 5; ++i)
+    if (a->o_stride[i] <= 0 || a->o_stride[i] % 8 != 0)
+      return fail(VX_EINVAL, "o stride[%d] must be a positive multiple of 8 elements", i);
+
+  const int lim[3] = {a->T, a->H, a->W};
+  const int ksz[3] = {std::min(a->kernel_t, a->T), std::min(a->kernel_h, a->H),
+                      std::min(a->kernel_w, a->W)};
+  NaChoice ch;
+  if (a->q_box[0] == 0 && a->q_box[1] == 0 && a->q_box[2] == 0) {
+    ch = na_choose_tiling(lim, ksz);
+  } else {
+    for (int i = 0; i < 3; ++i) {
+      if (!is_pow2(a->q_box[i])) return fail(VX_EINVAL, "q_box entries must be powers of two");
+      ch.qbox[i] = a->q_box[i];
+    }
+    if (ch.qbox[0] * ch.qbox[1] * ch.qbox[2] != 128) return fail(VX_EINVAL, "q_box must hold 128 queries");
+    if (a->pair_axis < 0 || a->pair_axis > 2) return fail(VX_EINVAL, "pair_axis must be 0, 1 or 2");
+    ch.pair = a->pair_axis;
+  }
+
+  int dev;
+  int rc = current_device(&dev);
+  if (rc != VX_OK) return rc;
+  int* status = nullptr;
+  if ((rc = status_word(dev, &status)) != VX_OK) return rc;
+
+  const int kv_box[3] = {kNaKT, kNaKH, kNaKW};
+  CUtensorMap tq, tk, tv;
+  if ((rc = na_tmap(&tq, "q", a->q, a->q_stride, a->batch, a->T, a->H, a->W, a->heads, kHeadDim, ch.qbox)) != VX_OK)
+    return rc;
+  if ((rc = na_tmap(&tk, "k", a->k, a->k_stride, a->batch, a->T, a->H, a->W, a->heads_kv, kHeadDim, kv_box)) != VX_OK)
+    return rc;
+  if ((rc = na_tmap(&tv, "v", a->v, a->v_stride, a->batch, a->T, a->H, a->W, a->heads_kv, kHeadDim, kv_box)) != VX_OK)
+    return rc;
+
+  NaParams p;
+  p.o = static_cast<__nv_bfloat16*>(a->o);
+  p.o_sb = a->o_stride[0];
+  p.o_st = a->o_stride[1];
+  p.o_sh = a->o_stride[2];
+  p.o_sw = a->o_stride[3];
+  p.o_shead = a->o_stride[4];
+  p.status = status;
+  p.B = a->batch;
+  p.T = a->T;
+  p.H = a->H;
+  p.W = a->W;
+  p.NH = a->heads;
+  p.NHkv = a->heads_kv;
+  p.kt = ksz[0];
+  p.kh = ksz[1];
+  p.kw = ksz[2];
+  long long n_regions = 1;
+  for (int i = 0; i < 3; ++i) {
+    p.qbox[i] = ch.qbox[i];
+    const int rsz = ch.qbox[i] * (i == ch.pair ? 2 : 1);
+    p.regions[i] = (lim[i] + rsz - 1) / rsz;
+    n_regions *= p.regions[i];
+  }
+  if (n_regions > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "grid too large");
+  p.pair_axis = ch.pair;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.round_logits = a->round_logits ? 1 : 0;
+
+  auto kern = attn_fwd_kernel<NaGeoDefault>;
+  if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
+  dim3 grid(static_cast<unsigned>(n_regions), a->heads, a->batch);
+  kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "na3d_fwd launch");
   return VX_OK;
 }
 

@@ -1,0 +1,122 @@
+"""3-D neighborhood attention on B200 (sm_100a), vidax's NA primitive.
+
+Mirrors `vidax.models.ltx2_5.diffusion_vae.neighborhood_attention_3d(q, k, v,
+kernel_size)` (src/vidax/models/ltx2_5/diffusion_vae.py:179-234): q, k, v are
+(B, T, H, W, NH, HD), q already scaled by the caller (diffusion_vae.py:265),
+windows are NATTEN's clamped ("shifted") windows of `_window_start`
+(diffusion_vae.py:152-164). The whole primitive is one launch of the
+neighborhood variant of the tcgen05 attention kernel.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+
+
+class Na3dArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("q_stride", ctypes.c_int64 * 5),
+        ("k_stride", ctypes.c_int64 * 5),
+        ("v_stride", ctypes.c_int64 * 5),
+        ("o_stride", ctypes.c_int64 * 5),
+        ("batch", ctypes.c_int32),
+        ("T", ctypes.c_int32),
+        ("H", ctypes.c_int32),
+        ("W", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("heads_kv", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("kernel_t", ctypes.c_int32),
+        ("kernel_h", ctypes.c_int32),
+        ("kernel_w", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("round_logits", ctypes.c_int32),
+        ("q_box", ctypes.c_int32 * 3),
+        ("pair_axis", ctypes.c_int32),
+    ]
+
+
+def window_start(length: int, kernel: int) -> np.ndarray:
+    """Per-index window start along one axis, computed by the library
+    (the `_window_start` contract, diffusion_vae.py:152-164)."""
+    out = (ctypes.c_int32 * length)()
+    lib = _lib.load()
+    fn = lib.vx_na3d_window_start
+    fn.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
+    fn.restype = ctypes.c_int
+    _lib.check(fn(length, kernel, out))
+    return np.frombuffer(out, dtype=np.int32).copy()
+
+
+def _check6(name: str, t: torch.Tensor) -> None:
+    if t.dim() != 6:
+        raise ValueError(f"{name} must be (B, T, H, W, NH, HD), got {tuple(t.shape)}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this implementation has no CPU path)")
+    if t.dtype != torch.bfloat16:
+        raise NotImplementedError(f"{name}.dtype={t.dtype}: the sm_100a kernel takes bfloat16")
+
+
+def _ready(t: torch.Tensor) -> torch.Tensor:
+    st = t.stride()
+    ok = (st[5] == 1 and t.data_ptr() % 16 == 0 and all(s > 0 and s % 8 == 0 for s in st[:5])
+          and (t.shape[0] == 1 or st[0] == t.shape[1] * st[1]))
+    return t if ok else t.contiguous()
+
+
+def neighborhood_attention_3d(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kernel_size: Sequence[int],
+    *, scale: float = 1.0, round_logits: bool = False,
+    q_box: Optional[Tuple[int, int, int]] = None, pair_axis: int = 0,
+) -> torch.Tensor:
+    """3-D neighborhood attention over (B, T, H, W, NH, HD) bf16 tensors.
+
+    Returns (B, T, H, W, NH, HD). `scale` multiplies q.k (vidax pre-scales q,
+    hence 1.0). `round_logits=True` rounds each q.k to bf16 before the fp32
+    softmax, as the reference's bf16 einsum does (diffusion_vae.py:222).
+    `q_box` / `pair_axis` override the kernel's query tiling (tuning only).
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check6(name, t)
+    B, T, H, W, NH, HD = q.shape
+    if k.shape[:4] != q.shape[:4] or v.shape != k.shape or k.shape[5] != HD:
+        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} disagree")
+    kt, kh, kw = (int(x) for x in kernel_size)
+    q, k, v = _ready(q), _ready(k), _ready(v)
+    out = torch.empty((B, T, H, W, NH, HD), dtype=torch.bfloat16, device=q.device)
+    a = Na3dArgs()
+    a.q, a.k, a.v, a.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    for dst, t in ((a.q_stride, q), (a.k_stride, k), (a.v_stride, v), (a.o_stride, out)):
+        for i in range(5):
+            dst[i] = t.stride(i)
+    a.batch, a.T, a.H, a.W = B, T, H, W
+    a.heads, a.heads_kv, a.head_dim = NH, k.shape[4], HD
+    a.kernel_t, a.kernel_h, a.kernel_w = kt, kh, kw
+    a.scale = float(scale)
+    a.round_logits = 1 if round_logits else 0
+    if q_box is not None:
+        a.q_box[0], a.q_box[1], a.q_box[2] = q_box
+        a.pair_axis = pair_axis
+    lib = _lib.load()
+    fn = lib.vx_na3d_fwd
+    fn.argtypes = [ctypes.POINTER(Na3dArgs), ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    with torch.cuda.device(q.device):
+        s = torch.cuda.current_stream(q.device)
+        _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)))
+    return out
+
+
+def na3d_flops(B: int, T: int, H: int, W: int, NH: int, HD: int, kernel_size) -> float:
+    """Algorithmic FLOPs, 4 * queries * |window| * HD * NH (window clamped to the grid)."""
+    kt, kh, kw = (min(a, b) for a, b in zip(kernel_size, (T, H, W)))
+    return 4.0 * B * T * H * W * kt * kh * kw * HD * NH

@@ -1,0 +1,229 @@
+"""DeepSpeed-Ulysses sequence-parallel attention on B200 (NCCL over NVLink).
+
+Mirrors the sequence-parallel half of `vidax.core.attention`:
+
+* `sequence_parallel_self_attention(q, k, v, sp_axis_name, scale=None)`
+  -- src/vidax/core/attention.py:341-388
+* `sequence_parallel_joint_self_attention(q, k, v, text_len, sp_axis_name, scale=None)`
+  -- src/vidax/core/attention.py:391-464
+
+vidax calls these inside `shard_map` with a bound mesh axis name. Here one
+process drives one GPU and the axis name is bound to a `torch.distributed`
+process group with `register_axis(name, group)` (the analogue of the mesh
+axis; `axis_index` / `axis_size` mirror `jax.lax.axis_index` and the mesh
+shape).
+
+Data path per batch item (rank r of P, local tokens S_loc, heads H):
+
+1. `vx_ulysses_pack` (one CUDA launch for q, k, v): strided (S_loc, H, D)
+   -> contiguous (P, S_loc, Hg, D), Hg = ceil(H / P), zero heads past H.
+2. three equal-split NCCL all-to-alls (tokens -> heads): rank r receives
+   (P_src, S_loc, Hg, D) == the full sequence (S, Hg, D) in natural token
+   order for its head group [r*Hg, (r+1)*Hg) -- the tiled
+   all_to_all(split_axis=2, concat_axis=1) of attention.py:379-381.
+3. the sm_100a attention kernel over (1, S, Hg, D), written in place as
+   (P, S_loc, Hg, D) -- already the heads -> tokens send layout.
+4. one NCCL all-to-all back (attention.py:388) and `vx_ulysses_unpack`
+   into the strided (S_loc, H, D) output, dropping padded heads.
+
+Unlike the reference (whose tiled all_to_all requires H % P == 0), head
+counts that do not divide P are padded with zero heads.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .attention import flash_attention
+
+_AXES: Dict[str, Optional["dist.ProcessGroup"]] = {}
+
+#: When set to a list, (start, end) CUDA events bracketing every attention
+#: kernel launch of the sequence-parallel path are appended to it (kernel-level
+#: timing for benchmarks; the data path is unchanged).
+KERNEL_EVENTS: Optional[list] = None
+
+
+def register_axis(name: str, group=None) -> None:
+    """Binds mesh axis `name` to a torch.distributed process group (None =
+    the default world group)."""
+    _AXES[name] = group
+
+
+def unregister_axis(name: str) -> None:
+    _AXES.pop(name, None)
+
+
+def _group(name: str):
+    if name not in _AXES:
+        raise NameError(
+            f"unbound axis name {name!r}: call vidax_b200.register_axis({name!r}, group) first "
+            "(the analogue of running inside shard_map over a mesh with that axis)")
+    return _AXES[name]
+
+
+def axis_size(name: str) -> int:
+    return dist.get_world_size(_group(name))
+
+
+def axis_index(name: str) -> int:
+    """This process's index along axis `name` (jax.lax.axis_index)."""
+    return dist.get_rank(_group(name))
+
+
+# ---------------------------------------------------------------- packing
+class HeadSlabArgs(ctypes.Structure):
+    _fields_ = [
+        ("num_tensors", ctypes.c_int32),
+        ("src", ctypes.c_void_p * 3),
+        ("dst", ctypes.c_void_p * 3),
+        ("stride", (ctypes.c_int64 * 2) * 3),
+        ("seq", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("groups", ctypes.c_int32),
+    ]
+
+
+def _slab_call(fn_name: str, strided, packed, heads: int, groups: int) -> None:
+    """strided: list of (S_loc, H, D) views; packed: list of contiguous
+    (groups, S_loc, Hg, D) buffers."""
+    a = HeadSlabArgs()
+    a.num_tensors = len(strided)
+    seq, _, d = strided[0].shape
+    for i, (s_t, p_t) in enumerate(zip(strided, packed)):
+        if not p_t.is_contiguous():
+            raise ValueError("packed side must be contiguous")
+        if s_t.stride(-1) != 1:
+            raise ValueError("head_dim must be contiguous")
+        if fn_name == "vx_ulysses_pack":
+            a.src[i], a.dst[i] = s_t.data_ptr(), p_t.data_ptr()
+        else:
+            a.src[i], a.dst[i] = p_t.data_ptr(), s_t.data_ptr()
+        a.stride[i][0], a.stride[i][1] = s_t.stride(0), s_t.stride(1)
+    a.seq, a.heads, a.head_dim, a.groups = seq, heads, d, groups
+    lib = _lib.load()
+    fn = getattr(lib, fn_name)
+    fn.argtypes = [ctypes.POINTER(HeadSlabArgs), ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    stream = torch.cuda.current_stream(strided[0].device)
+    _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)))
+
+
+def pack_heads(strided, groups: int, out=None):
+    """(S_loc, H, D) strided views (1-3 tensors) -> contiguous (groups, S_loc, Hg, D)."""
+    seq, heads, d = strided[0].shape
+    hg = -(-heads // groups)
+    if out is None:
+        out = [torch.empty((groups, seq, hg, d), dtype=t.dtype, device=t.device) for t in strided]
+    _slab_call("vx_ulysses_pack", list(strided), list(out), heads, groups)
+    return out
+
+
+def unpack_heads(packed, strided_out, heads: int) -> None:
+    """contiguous (groups, S_loc, Hg, D) -> strided (S_loc, H, D) views, in place."""
+    groups = packed[0].shape[0]
+    _slab_call("vx_ulysses_unpack", list(strided_out), list(packed), heads, groups)
+
+
+# ---------------------------------------------------------------- exchange
+def exchange(send: torch.Tensor, group, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Equal-split all-to-all along dim 0 (size P): chunk j of `send` goes to
+    rank j; chunk i of the result came from rank i (source-rank order)."""
+    recv = torch.empty_like(send) if out is None else out
+    dist.all_to_all_single(recv, send, group=group)
+    return recv
+
+
+def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int]):
+    """One batch item: qb/kb/vb/ob are (S_loc, H, D) views."""
+    S_loc, H, D = qb.shape
+    sq, sk, sv = pack_heads([qb, kb, vb], P)
+    rq, rk, rv = exchange(sq, group), exchange(sk, group), exchange(sv, group)
+    Hg = rq.shape[2]
+    S = P * S_loc
+    kv_len = None
+    if kv_valid is not None and kv_valid < S:
+        kv_len = torch.full((1,), kv_valid, dtype=torch.int32, device=qb.device)
+    events = KERNEL_EVENTS
+    if events is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    o_full = flash_attention(rq.view(1, S, Hg, D), rk.view(1, S, Hg, D), rv.view(1, S, Hg, D),
+                             sm_scale, kv_len=kv_len)
+    if events is not None:
+        e1.record()
+        events.append((e0, e1))
+    ro = exchange(o_full.view(P, S_loc, Hg, D), group)
+    unpack_heads([ro], [ob], H)
+
+
+def sequence_parallel_self_attention(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+    sp_axis_name: str, scale: Optional[float] = None,
+    *, valid_len: Optional[int] = None,
+) -> torch.Tensor:
+    """DeepSpeed-Ulysses self-attention (attention.py:341-388).
+
+    q, k, v: (B, L_local, H, D) -- this rank's contiguous token chunk
+    (`chunk_by_rank` ownership: rank r holds tokens [r*L_local, (r+1)*L_local)),
+    all heads. Returns (B, L_local, H, D). `valid_len` (extension): number
+    of real tokens in the global sequence when the caller padded it to a
+    multiple of the axis size; padded keys are then masked.
+    """
+    group = _group(sp_axis_name)
+    P = dist.get_world_size(group)
+    head_dim = q.shape[-1]
+    sm_scale = head_dim ** -0.5 if scale is None else scale
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError("self-attention needs q, k, v of equal shape")
+    out = torch.empty_like(q)
+    for b in range(q.shape[0]):
+        _ulysses_one(q[b], k[b], v[b], out[b], group, P, sm_scale, valid_len)
+    return out
+
+
+def sequence_parallel_joint_self_attention(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+    text_len: int, sp_axis_name: str, scale: Optional[float] = None,
+) -> torch.Tensor:
+    """Joint [text; visual] Ulysses attention (attention.py:391-464).
+
+    q, k, v: (B, text_len + L_vis_local, H, D): the text prefix replicated on
+    every rank, the visual tokens this rank's chunk. Only visual tokens go
+    through the all-to-all; the text q/k/v are sliced to this rank's head
+    group, joint attention runs over [text(full); visual(full)] for that
+    group, the visual output goes back through the reverse all-to-all and the
+    text output is all-gathered over heads.
+    """
+    group = _group(sp_axis_name)
+    P = dist.get_world_size(group)
+    r = dist.get_rank(group)
+    B, L, H, D = q.shape
+    sm_scale = D ** -0.5 if scale is None else scale
+    S_loc = L - text_len
+    Hg = -(-H // P)
+    h0, h1 = r * Hg, min((r + 1) * Hg, H)
+    out = torch.empty_like(q)
+    for b in range(B):
+        packed = pack_heads([q[b, text_len:], k[b, text_len:], v[b, text_len:]], P)
+        joint = []
+        for t_full, t_send in zip((q[b], k[b], v[b]), packed):
+            # [text rows of this head group ; received visual rows (P, S_loc, Hg, D)]
+            buf = torch.zeros((text_len + P * S_loc, Hg, D), dtype=q.dtype, device=q.device)
+            if h1 > h0:
+                buf[:text_len, : h1 - h0].copy_(t_full[:text_len, h0:h1])
+            exchange(t_send, group, out=buf[text_len:].view(P, S_loc, Hg, D))
+            joint.append(buf.unsqueeze(0))
+        o_j = flash_attention(joint[0], joint[1], joint[2], sm_scale)[0]
+        ro = exchange(o_j[text_len:].reshape(P, S_loc, Hg, D), group)
+        unpack_heads([ro], [out[b, text_len:]], H)
+        txt = o_j[:text_len].contiguous()
+        gathered = torch.empty((P, text_len, Hg, D), dtype=q.dtype, device=q.device)
+        dist.all_gather_into_tensor(gathered, txt, group=group)
+        unpack_heads([gathered], [out[b, :text_len]], H)
+    return out
