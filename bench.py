@@ -41,10 +41,11 @@ sys.path.insert(0, ROOT)
 B, S_GLOBAL, H, D = 1, 75600, 40, 128
 WORKLOAD = "cfg3: Ulysses self-attention layer, Wan2.1-14B 720p/81f (B=1, S=75600, H=40, D=128, bf16)"
 FALLBACK_PEAK_TFLOPS = 1590.0
-# dram__bytes_read.sum + dram__bytes_write.sum per head per query row per key
-# row, measured with ncu on attn_fwd_kernel (profiles/attn_fwd_cfg2_h4.md) and
-# scaled by units (heads x q-blocks x kv-tiles) to a full launch.
-TRAFFIC_BYTES_PER_HEAD_QK = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one attn_fwd_kernel launch
+# per (head x token), from the ncu capture of the (1, 32760, 8, 128) case
+# (profiles/attn_fwd_dense_h8.md: 248.6 MB / (8 x 32760)); traffic grows with
+# heads x tokens, so it scales to a full launch.
+TRAFFIC_BYTES_PER_HEAD_TOKEN = 948.6
 
 
 def flops(b, h, sq, sk, d):
@@ -151,6 +152,80 @@ def cpu_sample(seconds: float, rows_per_chunk: int = 256):
     desc = (f"numpy oracle, head 0 of cfg3: {done_rows} query rows x {S_GLOBAL} keys "
             f"({flops(1, 1, done_rows, S_GLOBAL, D) / 1e9:.1f} GFLOP in {dt:.1f} s)")
     return tf, threads, desc
+
+
+def time_launches(fn, steps: int, warmup: int):
+    """Device time (ms) per launch of `fn`, CUDA events on the current stream."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def kernel_case(name: str, dev):
+    """Named single-kernel cases (profiling and secondary measurements).
+
+    attn:B,S,H    dense attention, N(0,1) inputs, D=128
+    cfg2          BASELINE config 2: (1, 32760, 40, 128), per-head factors U[0.5, 2]
+    cfg4          BASELINE config 4: NA over (1, 21, 30, 52, 24, 128), window 5x9x9
+    na3d:T,H,W,NH window 5x9x9
+    Returns (callable, algorithmic FLOPs per launch, description).
+    """
+    import torch
+    import vidax_b200 as vx
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12345)
+
+    def rnd(shape):
+        return torch.randn(shape, generator=gen, device=dev, dtype=torch.float32).bfloat16()
+
+    if name == "cfg2" or name.startswith("attn:"):
+        if name == "cfg2":
+            b, s, h = 1, 32760, 40
+        else:
+            b, s, h = (int(x) for x in name.split(":")[1].split(","))
+        q, k, v = rnd((b, s, h, D)), rnd((b, s, h, D)), rnd((b, s, h, D))
+        if name == "cfg2":
+            f = torch.empty(3, h, device=dev).uniform_(0.5, 2.0, generator=gen)
+            q = (q.float() * f[0, :, None]).bfloat16()
+            k = (k.float() * f[1, :, None]).bfloat16()
+            v = (v.float() * f[2, :, None]).bfloat16()
+        return (lambda: vx.flash_attention(q, k, v, D ** -0.5)), flops(b, h, s, s, D), \
+            f"attention (B={b}, S={s}, H={h}, D={D})"
+    if name == "cfg4" or name.startswith("na3d:"):
+        if name == "cfg4":
+            t, hh, w, nh = 21, 30, 52, 24
+        else:
+            t, hh, w, nh = (int(x) for x in name.split(":")[1].split(","))
+        shape = (1, t, hh, w, nh, D)
+        q = (rnd(shape).float() * D ** -0.5).bfloat16()
+        k, v = rnd(shape), rnd(shape)
+        fl = vx.na3d_flops(1, t, hh, w, nh, D, (5, 9, 9))
+        return (lambda: vx.neighborhood_attention_3d(q, k, v, (5, 9, 9))), fl, \
+            f"neighborhood attention (1, {t}, {hh}, {w}, {nh}, {D}), window 5x9x9"
+    raise SystemExit(f"unknown --kernel-only case {name!r}")
+
+
+def run_kernel_only(args):
+    import torch
+    from vidax_b200 import _lib
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    fn, fl, desc = kernel_case(args.kernel_only, dev)
+    ms = time_launches(fn, args.steps, args.warmup)
+    assert _lib.device_status() == 0
+    print(json.dumps({"case": args.kernel_only, "desc": desc, "ms_per_launch": round(ms, 4),
+                      "tflops": round(fl / (ms / 1e3) / 1e12, 2), "launches": args.steps}),
+          flush=True)
 
 
 def run_reference(args, rank: int):
@@ -309,6 +384,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     h2d = 3 * B * s_loc * H * D * elem
     d2h = B * s_loc * H * D * elem
 
+    secondary = {}
+    if world == 1 and not args.no_secondary:
+        burst_peak = load_peaks()[0]
+        for case in ("cfg2", "cfg4"):
+            fn, fl, desc = kernel_case(case, dev)
+            kms = time_launches(fn, 5 if case == "cfg2" else 20, 3)
+            tf = fl / (kms / 1e3) / 1e12
+            secondary[case] = {"desc": desc, "ms": round(kms, 4), "tflops": round(tf, 2),
+                               "frac_of_burst_peak": round(tf / burst_peak, 4)}
+        assert _lib.device_status() == 0
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, desc = cpu_sample(args.cpu_seconds)
@@ -320,8 +406,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if rank != 0:
         return
     traffic = None
-    if TRAFFIC_BYTES_PER_HEAD_QK is not None:
-        traffic = TRAFFIC_BYTES_PER_HEAD_QK * B * hg * S_GLOBAL * S_GLOBAL
+    if TRAFFIC_BYTES_PER_HEAD_TOKEN is not None:
+        traffic = round(TRAFFIC_BYTES_PER_HEAD_TOKEN * B * hg * S_GLOBAL)
     peak = sustained if sustained else burst
     line = {
         "metric": "attention TFLOP/s (Ulysses attn layer, Wan2.1-14B 720p)",
@@ -346,6 +432,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if secondary:
+        line["secondary"] = secondary
     if world > 1:
         a2a_bytes = 4 * (world - 1) / world * B * s_loc * hg * world * D * elem
         line["a2a"] = {"bytes_sent_per_gpu": a2a_bytes,
@@ -361,6 +449,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the extra cfg2 / cfg4 single-kernel measurements")
+    ap.add_argument("--kernel-only", default=None,
+                    help="time one kernel case (cfg2, cfg4, attn:B,S,H, na3d:T,H,W,NH) and exit")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -370,6 +462,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.kernel_only:
+        run_kernel_only(args)
         return
     if world > 1:
         import torch

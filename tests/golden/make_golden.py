@@ -1,0 +1,251 @@
+"""Generates tests/golden/*.npz by running the reference's own Python code.
+
+JAX/Flax are not installed here, so the reference modules cannot be imported
+as a whole. Instead this script reads the reference sources, extracts the
+functions on the attention hot path with `ast`, and executes them unchanged
+in a namespace where `jax` / `jnp` are a small numpy shim:
+
+* src/vidax/models/ltx2_5/diffusion_vae.py: `_window_start`, `_gather_window`,
+  `neighborhood_attention_3d` (lines 152-234);
+* src/vidax/core/attention.py: `chunk_by_rank`, `local_attention`,
+  `dot_product_attention`, `sequence_parallel_self_attention` (lines
+  132-146, 321-388, 467-533), run on P threads (one per emulated device)
+  whose `jax.lax.all_to_all` / `axis_index` meet at a barrier.
+
+The shim restates the third-party jax primitives the code calls: `jnp.take`,
+`jnp.moveaxis`, `jnp.einsum` (bf16 operands, f32 accumulation, result in the
+operand dtype, as XLA does), `jax.nn.softmax`, `jax.lax.scan`, `jax.vmap`,
+`jax.lax.all_to_all(tiled=True)`, and `jax.nn.dot_product_attention` (f32
+logits, f32 softmax, weights cast to the input dtype, bf16 einsum). The
+vidax code around them -- window starts, gather indices, key ordering, the
+scan/vmap structure, dtype handling, dispatch, default scale and the Ulysses
+split/concat axes -- is the reference's own.
+
+Run from the repository root, where /root/reference exists:
+    python tests/golden/make_golden.py
+The fixtures are committed; tests only read them (the reference does not
+exist on the GPU box).
+"""
+from __future__ import annotations
+
+import ast
+import os
+import sys
+import threading
+import types
+
+import ml_dtypes
+import numpy as np
+
+REF = os.environ.get("VIDAX_REFERENCE", "/root/reference")
+OUT_DIR = os.path.dirname(os.path.abspath(__file__))
+BF16 = ml_dtypes.bfloat16
+
+
+# ----------------------------------------------------------------- jax shim
+def _einsum(spec, *ops, **kw):
+    dt = np.result_type(*[o.dtype for o in ops])
+    res = np.einsum(spec, *[np.asarray(o, np.float32) for o in ops], optimize=True)
+    return res.astype(dt)
+
+
+def _softmax(x, axis=-1):
+    x = np.asarray(x)
+    m = x.max(axis=axis, keepdims=True)
+    e = np.exp(x - m)
+    return (e / e.sum(axis=axis, keepdims=True)).astype(x.dtype)
+
+
+def _scan(f, init, xs):
+    n = len(xs[0]) if isinstance(xs, (tuple, list)) else len(xs)
+    carry, ys = init, []
+    for i in range(n):
+        x_i = tuple(x[i] for x in xs) if isinstance(xs, (tuple, list)) else xs[i]
+        carry, y = f(carry, x_i)
+        ys.append(y)
+    return carry, np.stack(ys)
+
+
+def _vmap(f, in_axes=0, out_axes=0):
+    def g(x):
+        outs = [f(np.take(x, i, axis=in_axes)) for i in range(x.shape[in_axes])]
+        return np.stack(outs, axis=out_axes)
+    return g
+
+
+def _dot_product_attention(q, k, v, bias=None, mask=None, scale=None, **kw):
+    dt = q.dtype
+    D = q.shape[-1]
+    scale = D ** -0.5 if scale is None else scale
+    logits = np.einsum("btnh,bsnh->bnts", np.asarray(q, np.float32), np.asarray(k, np.float32))
+    logits = logits * np.float32(scale)
+    if bias is not None:
+        logits = logits + np.asarray(bias, np.float32)
+    if mask is not None:
+        logits = np.where(mask, logits, np.float32(-0.7 * np.finfo(np.float32).max))
+    p = _softmax(logits.astype(np.float32), axis=-1).astype(dt)
+    out = np.einsum("bnts,bsnh->btnh", np.asarray(p, np.float32), np.asarray(v, np.float32))
+    return out.astype(dt)
+
+
+class _Device:
+    platform = "cpu"
+    device_kind = "cpu"
+
+
+class _Collective:
+    """Thread-per-device stand-in for a mesh axis: all_to_all / axis_index."""
+
+    def __init__(self, P):
+        self.P = P
+        self.barrier = threading.Barrier(P)
+        self.slots = [None] * P
+        self.local = threading.local()
+
+    def axis_index(self, name):
+        return self.local.rank
+
+    def all_to_all(self, x, axis_name, split_axis, concat_axis, tiled=False):
+        assert tiled
+        r = self.local.rank
+        self.slots[r] = np.split(np.asarray(x), self.P, axis=split_axis)
+        self.barrier.wait()
+        res = np.concatenate([self.slots[src][r] for src in range(self.P)], axis=concat_axis)
+        self.barrier.wait()
+        return res
+
+    def dynamic_slice_in_dim(self, x, start, size, axis=0):
+        return np.take(x, np.arange(int(start), int(start) + size), axis=axis)
+
+
+def make_namespace(coll=None):
+    jnp = types.SimpleNamespace(
+        take=lambda a, idx, axis=None: np.take(a, np.asarray(idx), axis=axis),
+        moveaxis=np.moveaxis, asarray=np.asarray, einsum=_einsum,
+        promote_types=np.promote_types, float32=np.float32, bfloat16=BF16,
+        ndarray=np.ndarray, pad=np.pad, where=np.where, arange=np.arange,
+        broadcast_to=np.broadcast_to, transpose=np.transpose, concatenate=np.concatenate)
+    lax = types.SimpleNamespace(scan=_scan)
+    if coll is not None:
+        lax.all_to_all = coll.all_to_all
+        lax.axis_index = coll.axis_index
+        lax.dynamic_slice_in_dim = coll.dynamic_slice_in_dim
+    else:
+        lax.dynamic_slice_in_dim = lambda x, s, n, axis=0: np.take(
+            x, np.arange(int(s), int(s) + n), axis=axis)
+    jax = types.SimpleNamespace(
+        lax=lax, vmap=_vmap, nn=types.SimpleNamespace(
+            softmax=_softmax, dot_product_attention=_dot_product_attention),
+        devices=lambda: [_Device()], device_count=lambda: 1)
+    from typing import Optional, Tuple
+    return {"jax": jax, "jnp": jnp, "np": np, "Optional": Optional, "Tuple": Tuple,
+            "Mesh": object, "P": lambda *a: a}
+
+
+def load_functions(relpath, names, ns):
+    path = os.path.join(REF, relpath)
+    src = open(path).read()
+    tree = ast.parse(src)
+    for node in tree.body:
+        if isinstance(node, ast.FunctionDef) and node.name in names:
+            seg = ast.get_source_segment(src, node)
+            exec(compile("\n" * (node.lineno - 1) + seg, path, "exec"), ns)
+    missing = [n for n in names if n not in ns]
+    if missing:
+        raise RuntimeError(f"functions {missing} not found in {path}")
+    return ns
+
+
+# ----------------------------------------------------------------- fixtures
+def seeded(shape, seed, scale=None):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = rng.standard_normal(shape, dtype=np.float32)
+    if scale is not None:
+        x = x * np.float32(scale)
+    return x.astype(BF16)
+
+
+def gen_na3d():
+    ns = load_functions("src/vidax/models/ltx2_5/diffusion_vae.py",
+                        ["_window_start", "_gather_window", "neighborhood_attention_3d"],
+                        make_namespace())
+    out = {}
+    # window starts for every (length, kernel) in a grid of small sizes
+    lens, kers, starts = [], [], []
+    for L in range(1, 40):
+        for kk in range(1, 14):
+            s = np.asarray(ns["_window_start"](L, kk), np.int64)
+            lens.append(L)
+            kers.append(kk)
+            starts.append(np.pad(s, (0, 40 - L), constant_values=-1))
+    out["ws_length"] = np.array(lens, np.int32)
+    out["ws_kernel"] = np.array(kers, np.int32)
+    out["ws_start"] = np.array(starts, np.int32)
+    cases = [((1, 3, 5, 7, 2, 16), (3, 3, 5)), ((1, 4, 6, 9, 1, 32), (3, 5, 5)),
+             ((2, 2, 3, 4, 1, 8), (5, 9, 9)), ((1, 5, 4, 6, 2, 16), (3, 7, 7)),
+             ((1, 3, 5, 9, 2, 128), (3, 3, 5)), ((1, 4, 7, 10, 1, 128), (5, 9, 9))]
+    for i, (shape, kernel) in enumerate(cases):
+        q = seeded(shape, 40 + i, scale=shape[-1] ** -0.5)
+        k = seeded(shape, 50 + i)
+        v = seeded(shape, 60 + i)
+        o = ns["neighborhood_attention_3d"](q, k, v, kernel)
+        assert o.dtype == BF16 and o.shape == shape
+        out[f"na{i}_q"], out[f"na{i}_k"], out[f"na{i}_v"] = (x.astype(np.float32) for x in (q, k, v))
+        out[f"na{i}_o"] = o.astype(np.float32)
+        out[f"na{i}_kernel"] = np.array(kernel, np.int32)
+    return out
+
+
+def gen_attention():
+    names = ["chunk_by_rank", "local_attention", "dot_product_attention",
+             "sequence_parallel_self_attention"]
+    out = {}
+    ns = load_functions("src/vidax/core/attention.py", names, make_namespace())
+    # dot_product_attention on the CPU path: default scale and explicit scale
+    q, k, v = seeded((2, 37, 3, 16), 70), seeded((2, 29, 3, 16), 71), seeded((2, 29, 3, 16), 72)
+    out["dpa_q"], out["dpa_k"], out["dpa_v"] = (x.astype(np.float32) for x in (q, k, v))
+    out["dpa_o_default"] = ns["dot_product_attention"](q, k, v).astype(np.float32)
+    out["dpa_o_scale1"] = ns["dot_product_attention"](q, k, v, scale=1.0).astype(np.float32)
+    out["local_o"] = ns["local_attention"](q, k, v).astype(np.float32)
+    # head_dim 128 (the sm_100a kernel's size): self- and cross-attention
+    q, k, v = seeded((1, 300, 2, 128), 73), seeded((1, 300, 2, 128), 74), seeded((1, 300, 2, 128), 75)
+    out["dpa128_q"], out["dpa128_k"], out["dpa128_v"] = (x.astype(np.float32) for x in (q, k, v))
+    out["dpa128_o"] = ns["dot_product_attention"](q, k, v).astype(np.float32)
+    kx, vx = seeded((1, 77, 2, 128), 76), seeded((1, 77, 2, 128), 77)
+    out["cross128_k"], out["cross128_v"] = kx.astype(np.float32), vx.astype(np.float32)
+    out["cross128_o"] = ns["local_attention"](q, kx, vx).astype(np.float32)
+    # Ulysses over P emulated devices, each holding its chunk_by_rank share
+    for P, (B, S, H, D) in ((2, (1, 16, 4, 8)), (4, (2, 24, 8, 8)), (8, (1, 256, 8, 128))):
+        coll = _Collective(P)
+        ns_p = load_functions("src/vidax/core/attention.py", names, make_namespace(coll))
+        qg, kg, vg = seeded((B, S, H, D), 80 + P), seeded((B, S, H, D), 90 + P), seeded((B, S, H, D), 100 + P)
+        results = [None] * P
+
+        def worker(r):
+            coll.local.rank = r
+            loc = [ns_p["chunk_by_rank"](x, 1, P, r) for x in (qg, kg, vg)]
+            results[r] = ns_p["sequence_parallel_self_attention"](*loc, "sp")
+
+        threads = [threading.Thread(target=worker, args=(r,)) for r in range(P)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        out[f"sp{P}_q"], out[f"sp{P}_k"], out[f"sp{P}_v"] = (x.astype(np.float32) for x in (qg, kg, vg))
+        out[f"sp{P}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
+    return out
+
+
+def main():
+    if not os.path.isdir(REF):
+        sys.exit(f"reference not found at {REF}")
+    na = gen_na3d()
+    np.savez_compressed(os.path.join(OUT_DIR, "na3d_reference.npz"), **na)
+    at = gen_attention()
+    np.savez_compressed(os.path.join(OUT_DIR, "attention_reference.npz"), **at)
+    for f in ("na3d_reference.npz", "attention_reference.npz"):
+        print(f, os.path.getsize(os.path.join(OUT_DIR, f)), "bytes")
+
+
+if __name__ == "__main__":
+    main()
