@@ -71,7 +71,9 @@ _lib = None
 
 
 def lib_path() -> str:
-    return _build.LIB_PATH
+    """The in-tree library, or VIDAX_B200_LIB when set (an alternative build
+    of the same sources, e.g. for tuning)."""
+    return os.environ.get("VIDAX_B200_LIB") or _build.LIB_PATH
 
 
 def load(build_if_missing: bool = True) -> ctypes.CDLL:
@@ -80,8 +82,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        path = _build.LIB_PATH
-        if build_if_missing and _build.is_stale():
+        path = lib_path()
+        if path == _build.LIB_PATH and build_if_missing and _build.is_stale():
             try:
                 _build.build()
             except RuntimeError:

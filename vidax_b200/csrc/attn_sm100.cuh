@@ -47,6 +47,22 @@ constexpr uint32_t kTileBytes = 128u * 128u * 2u;  // one 128x128 bf16 tile
 constexpr uint32_t kHalfBytes = kTileBytes / 2;     // 128 rows x 64 cols (128B rows)
 constexpr float kRescaleThreshold = 8.0f;
 
+// Softmax tuning knobs (compile-time): every kPolyEvery-th pair of
+// exponentials goes through the FMA-pipe polynomial (0 = all on MUFU);
+// kSplitP publishes P in two key halves so PV starts on the first half.
+#ifndef VX_POLY_EVERY
+#define VX_POLY_EVERY 0
+#endif
+#ifndef VX_SPLIT_P
+#define VX_SPLIT_P 1
+#endif
+#ifndef VX_PACKED_F32X2
+#define VX_PACKED_F32X2 0
+#endif
+constexpr int kPolyEvery = VX_POLY_EVERY;
+constexpr bool kSplitP = VX_SPLIT_P != 0;
+constexpr bool kPackedF32x2 = VX_PACKED_F32X2 != 0;
+
 constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
 constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
@@ -61,10 +77,11 @@ enum : int {
   kVFull = 6,      // kStages
   kVEmpty = 8,     // kStages
   kSFull = 10,     // 2
-  kPFull = 12,     // 2
-  kOFull = 14,     // 2
-  kDrain = 16,     // 1
-  kNumBars = 17,
+  kPLo = 12,       // 2: P columns for keys [0, 64) written
+  kPHi = 14,       // 2: P columns for keys [64, 128) written
+  kOFull = 16,     // 2
+  kDrain = 18,     // 1
+  kNumBars = 19,
 };
 constexpr uint32_t kTmemSlotOff = kSmemBar + 8 * kNumBars;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
@@ -77,24 +94,30 @@ __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); 
 
 // S_t = Q_t K^T over head_dim 128 (8 MMAs of K=16). Each operand tile is two
 // 128B-swizzled halves of 64 columns; within a half the K step advances the
-// descriptor start address by 32 bytes.
-__device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint32_t q_smem, uint32_t k_smem) {
+// descriptor start address by 32 bytes. `q_desc` / `k_desc` are the tiles'
+// base descriptors; the per-step offsets are compile-time constants added to
+// the start-address field (in 16-byte units, no carry out of the field since
+// shared memory is below 256 KB).
+__device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint64_t q_desc, uint64_t k_desc) {
 #pragma unroll
   for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-    mma_ss(tmem_s, sdesc_sw128(q_smem + off, 16, 1024), sdesc_sw128(k_smem + off, 16, 1024),
-           kIdescS, kk > 0 ? 1u : 0u);
+    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+    mma_ss(tmem_s, q_desc + off, k_desc + off, kIdescS, kk > 0 ? 1u : 0u);
   }
 }
 
 // O_t (+)= P_t V with P_t read from tensor memory (8 columns per K=16 step)
-// and V an N-major 128B-swizzled tile: 16 keys per step = 2048 bytes; the two
-// 64-column halves of head_dim are kHalfBytes apart (leading byte offset).
-__device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t v_smem,
-                                         bool accumulate) {
+// and V an N-major 128B-swizzled tile (`v_desc`): 16 keys per step = 2048
+// bytes; the two 64-column halves of head_dim are kHalfBytes apart (leading
+// byte offset). `half` selects keys [0, 64) or [64, 128) of the tile (4 MMAs
+// each), so the first half can run while the softmax still produces the
+// second.
+__device__ __forceinline__ void issue_pv_half(uint32_t tmem_o, uint32_t tmem_p, uint64_t v_desc,
+                                              int half, bool accumulate) {
 #pragma unroll
-  for (int kk = 0; kk < kBlockN / 16; ++kk) {
-    mma_ts(tmem_o, tmem_p + kk * 8, sdesc_sw128(v_smem + kk * 2048, kHalfBytes, 1024), kIdescO,
+  for (int k4 = 0; k4 < 4; ++k4) {
+    const int kk = half * 4 + k4;
+    mma_ts(tmem_o, tmem_p + kk * 8, v_desc + static_cast<uint64_t>((kk * 2048) >> 4), kIdescO,
            (accumulate || kk > 0) ? 1u : 0u);
   }
 }
@@ -133,7 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kSFull + t), 1);
-      mbar_init(bar(kPFull + t), 128);
+      mbar_init(bar(kPLo + t), 128);
+      mbar_init(bar(kPHi + t), 128);
       mbar_init(bar(kOFull + t), 1);
     }
     mbar_init(bar(kDrain), 1);
@@ -197,7 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // A query tile that does not need a KV tile skips it entirely (the
     // neighborhood geometry; the dense one needs every tile).
     if (lane == 0 && n_kv > 0) {
-      const uint32_t q_sm[2] = {sbase + kSmemQ, sbase + kSmemQ + kTileBytes};
+      const uint64_t q_desc[2] = {sdesc_sw128(sbase + kSmemQ, 16, 1024),
+                                  sdesc_sw128(sbase + kSmemQ + kTileBytes, 16, 1024)};
+      static_assert(kStages == 2, "descriptor selection below assumes two stages");
+      const uint64_t k_desc0 = sdesc_sw128(sbase + kSmemK, 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(sbase + kSmemV, kHalfBytes, 1024);
+      // stage 1 = stage 0 + kTileBytes in the start-address field
+      constexpr uint64_t kStageStep = kTileBytes >> 4;
       bool ok = mbar_wait(bar(kQFull + 0), 0, abort_flag, status, kDevTimeoutMma) &&
                 mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma) &&
                 mbar_wait(bar(kKFull + 0), 0, abort_flag, status, kDevTimeoutMma);
@@ -208,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (geo.needs(t, 0)) {
-            issue_qk(tmem + 128 * t, q_sm[t], sbase + kSmemK);
+            issue_qk(tmem + 128 * t, q_desc[t], k_desc0);
             tc_commit(bar(kSFull + t));
           }
         }
@@ -219,20 +249,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s1 = (j + 1) % kStages;
         const uint32_t ph1 = ((j + 1) / kStages) & 1;
         const bool has_next = j + 1 < n_kv;
-        const uint32_t v_sm = sbase + kSmemV + s * kTileBytes;
-        const uint32_t k_next = sbase + kSmemK + s1 * kTileBytes;
+        const uint64_t v_d = v_desc0 + (s ? kStageStep : 0);
+        const uint64_t k_next = k_desc0 + (s1 ? kStageStep : 0);
         tc_commit(bar(kKEmpty + s));  // every S(j) MMA was issued before this point
         if (!mbar_wait(bar(kVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
         bool k_next_ready = false;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (geo.needs(t, j)) {
-            if (!mbar_wait(bar(kPFull + t), pv_count[t] & 1, abort_flag, status, kDevTimeoutMma)) {
+            const uint32_t par = pv_count[t] & 1;
+            if (!mbar_wait(bar(kPLo + t), par, abort_flag, status, kDevTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            if (kSplitP) {
+              tc_fence_after();
+              issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, pv_count[t] > 0);
+            }
+            if (!mbar_wait(bar(kPHi + t), par, abort_flag, status, kDevTimeoutMma)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_pv(tmem + 256 + 128 * t, tmem + 128 * t, v_sm, pv_count[t] > 0);
+            if (!kSplitP)
+              issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, pv_count[t] > 0);
+            issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 1, true);
             ++pv_count[t];
             if (j == last[t]) tc_commit(bar(kOFull + t));
           }
@@ -245,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_fence_after();
               k_next_ready = true;
             }
-            issue_qk(tmem + 128 * t, q_sm[t], k_next);
+            issue_qk(tmem + 128 * t, q_desc[t], k_next);
             tc_commit(bar(kSFull + t));
           }
         }
@@ -287,15 +328,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       geo.mask_scores(j, sr);
 
+      // row max: 3-input max over 128 scores, 4 independent chains
       float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[c][i + 0]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[c][i + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(sr[c][i + 2]));
-          mx3 = fmaxf(mx3, __uint_as_float(sr[c][i + 3]));
+        for (int i = 0; i < 32; i += 8) {
+          mx0 = fmax3(mx0, __uint_as_float(sr[c][i + 0]), __uint_as_float(sr[c][i + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[c][i + 2]), __uint_as_float(sr[c][i + 3]));
+          mx2 = fmax3(mx2, __uint_as_float(sr[c][i + 4]), __uint_as_float(sr[c][i + 5]));
+          mx3 = fmax3(mx3, __uint_as_float(sr[c][i + 6]), __uint_as_float(sr[c][i + 7]));
         }
       }
       const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale_log2;
@@ -322,24 +364,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = m_new;
       }
       const float neg_m = (m_used == neg_inf()) ? 0.f : -m_used;
+      // p = 2^(s * scale_log2 - m): packed f32x2 FMA for the argument; one
+      // pair in four goes through the FMA-pipe polynomial, the rest through
+      // MUFU ex2. P is published in two halves (keys [0,64), [64,128)).
+      const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+      const uint64_t negm2 = f2_pack(neg_m, neg_m);
+      uint64_t lsum2 = f2_pack(0.f, 0.f);
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m));
-          const float e1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m));
-          ls0 += e0;
-          ls1 += e1;
+          float x0, x1, e0, e1;
+          if (kPackedF32x2) {
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c][2 * i]),
+                                               __uint_as_float(sr[c][2 * i + 1])),
+                                       scale2, negm2);
+            f2_unpack(x2, x0, x1);
+          } else {
+            x0 = fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m);
+            x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m);
+          }
+          if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
+            e0 = exp2_poly(x0);
+            e1 = exp2_poly(x1);
+          } else {
+            e0 = ex2_approx(x0);
+            e1 = ex2_approx(x1);
+          }
+          if (kPackedF32x2) {
+            lsum2 = f2_add(lsum2, f2_pack(e0, e1));
+          } else {
+            ls0 += e0;
+            ls1 += e1;
+          }
           pk[i] = pack_bf16x2(e0, e1);
         }
         tmem_st16(t_s + c * 16, pk);
+        if ((kSplitP && c == 1) || c == 3) {
+          tmem_wait_st();
+          tc_fence_before();
+          if (kSplitP) {
+            mbar_arrive(bar((c == 1 ? kPLo : kPHi) + wg));
+          } else {
+            mbar_arrive(bar(kPLo + wg));
+            mbar_arrive(bar(kPHi + wg));
+          }
+        }
       }
+      if (kPackedF32x2) f2_unpack(lsum2, ls0, ls1);
       l_sum += ls0 + ls1;
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(kPFull + wg));
       ++count;
     }
 
