@@ -54,7 +54,7 @@ constexpr float kRescaleThreshold = 8.0f;
 #define VX_POLY_EVERY 0
 #endif
 #ifndef VX_SPLIT_P
-#define VX_SPLIT_P 1
+#define VX_SPLIT_P 0
 #endif
 #ifndef VX_PACKED_F32X2
 #define VX_PACKED_F32X2 0
@@ -71,17 +71,16 @@ constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + barriers + alignmen
 
 // barrier slots
 enum : int {
-  kQFull = 0,      // 2
-  kKFull = 2,      // kStages
+  kQFull = 0,      // 2: [0] = Q0 + K(0), [1] = Q1
+  kKVFull = 2,     // kStages: V(j) + K(j+1) landed (stage j % kStages)
   kKEmpty = 4,     // kStages
-  kVFull = 6,      // kStages
-  kVEmpty = 8,     // kStages
-  kSFull = 10,     // 2
-  kPLo = 12,       // 2: P columns for keys [0, 64) written
-  kPHi = 14,       // 2: P columns for keys [64, 128) written
-  kOFull = 16,     // 2
-  kDrain = 18,     // 1
-  kNumBars = 19,
+  kVEmpty = 6,     // kStages
+  kSFull = 8,      // 2
+  kPLo = 10,       // 2: P columns for keys [0, 64) written (split publication)
+  kPHi = 12,       // 2: all P columns written
+  kOFull = 14,     // 2
+  kDrain = 16,     // 1
+  kNumBars = 17,
 };
 constexpr uint32_t kTmemSlotOff = kSmemBar + 8 * kNumBars;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
@@ -149,9 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(kQFull + 0), 1);
     mbar_init(bar(kQFull + 1), 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kKFull + s), 1);
+      mbar_init(bar(kKVFull + s), 1);
       mbar_init(bar(kKEmpty + s), 1);
-      mbar_init(bar(kVFull + s), 1);
       mbar_init(bar(kVEmpty + s), 1);
     }
     for (int t = 0; t < 2; ++t) {
@@ -180,34 +178,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
+    // Order: Q0 + K(0) on Q_FULL[0], Q1 on Q_FULL[1], then per KV tile j the
+    // pair V(j), K(j+1) on one KV_FULL barrier, so the MMA issuer waits once
+    // per KV tile for both operands it needs next.
     if (lane == 0 && n_kv > 0) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      for (int t = 0; t < 2; ++t) {
-        mbar_expect_tx(bar(kQFull + t), kTileBytes);
-        geo.load_q(&tm_q, t, sbase + kSmemQ + t * kTileBytes, bar(kQFull + t), pol_q);
-      }
-      int jk = -1, jv = -1;  // last K / V tile whose load was issued
+      mbar_expect_tx(bar(kQFull + 0), 2 * kTileBytes);
+      geo.load_q(&tm_q, 0, sbase + kSmemQ, bar(kQFull + 0), pol_q);
+      geo.load_kv(&tm_k, 0, sbase + kSmemK, bar(kQFull + 0), pol_kv);
+      mbar_expect_tx(bar(kQFull + 1), kTileBytes);
+      geo.load_q(&tm_q, 1, sbase + kSmemQ + kTileBytes, bar(kQFull + 1), pol_q);
+      int jl = -1;  // last KV tile whose V(j) / K(j+1) pair was issued
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(bar(kKEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) break;
-        mbar_expect_tx(bar(kKFull + s), kTileBytes);
-        geo.load_kv(&tm_k, j, sbase + kSmemK + s * kTileBytes, bar(kKFull + s), pol_kv);
-        jk = j;
+        const bool has_next = j + 1 < n_kv;
+        const int s1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
         if (!mbar_wait(bar(kVEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) break;
-        mbar_expect_tx(bar(kVFull + s), kTileBytes);
-        geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kVFull + s), pol_kv);
-        jv = j;
+        if (has_next &&
+            !mbar_wait(bar(kKEmpty + s1), ph1 ^ 1, abort_flag, status, kDevTimeoutLoad))
+          break;
+        mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kTileBytes : kTileBytes);
+        geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kKVFull + s), pol_kv);
+        if (has_next)
+          geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kTileBytes, bar(kKVFull + s), pol_kv);
+        jl = j;
       }
       if (*abort_flag) {
-        // Drain: wait for the most recent load into each stage to land so no
-        // TMA write targets this CTA's shared memory after it exits. Only the
-        // last load per stage can still be pending, so its parity is exact.
-        for (int j = jk; j >= 0 && j > jk - kStages; --j)
-          mbar_wait_drain(bar(kKFull + j % kStages), (j / kStages) & 1, status);
-        for (int j = jv; j >= 0 && j > jv - kStages; --j)
-          mbar_wait_drain(bar(kVFull + j % kStages), (j / kStages) & 1, status);
+        // Drain: wait for the most recent loads into each stage to land so
+        // no TMA write targets this CTA's shared memory after it exits. Only
+        // the last pair per stage can still be pending, so its parity is exact.
+        for (int j = jl; j >= 0 && j > jl - kStages; --j)
+          mbar_wait_drain(bar(kKVFull + j % kStages), (j / kStages) & 1, status);
         mbar_wait_drain(bar(kQFull + 0), 0, status);
         mbar_wait_drain(bar(kQFull + 1), 0, status);
       }
@@ -229,8 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // stage 1 = stage 0 + kTileBytes in the start-address field
       constexpr uint64_t kStageStep = kTileBytes >> 4;
       bool ok = mbar_wait(bar(kQFull + 0), 0, abort_flag, status, kDevTimeoutMma) &&
-                mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma) &&
-                mbar_wait(bar(kKFull + 0), 0, abort_flag, status, kDevTimeoutMma);
+                mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma);
       int last[2] = {geo.last_tile(0), geo.last_tile(1)};
       int pv_count[2] = {0, 0};
       if (ok) {
@@ -247,22 +250,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
         const int s1 = (j + 1) % kStages;
-        const uint32_t ph1 = ((j + 1) / kStages) & 1;
         const bool has_next = j + 1 < n_kv;
         const uint64_t v_d = v_desc0 + (s ? kStageStep : 0);
         const uint64_t k_next = k_desc0 + (s1 ? kStageStep : 0);
         tc_commit(bar(kKEmpty + s));  // every S(j) MMA was issued before this point
-        if (!mbar_wait(bar(kVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
-        bool k_next_ready = false;
+        if (!mbar_wait(bar(kKVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
+        tc_fence_after();
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (geo.needs(t, j)) {
             const uint32_t par = pv_count[t] & 1;
-            if (!mbar_wait(bar(kPLo + t), par, abort_flag, status, kDevTimeoutMma)) {
-              ok = false;
-              break;
-            }
             if (kSplitP) {
+              if (!mbar_wait(bar(kPLo + t), par, abort_flag, status, kDevTimeoutMma)) {
+                ok = false;
+                break;
+              }
               tc_fence_after();
               issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, pv_count[t] > 0);
             }
@@ -278,14 +280,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (j == last[t]) tc_commit(bar(kOFull + t));
           }
           if (has_next && geo.needs(t, j + 1)) {
-            if (!k_next_ready) {
-              if (!mbar_wait(bar(kKFull + s1), ph1, abort_flag, status, kDevTimeoutMma)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              k_next_ready = true;
-            }
             issue_qk(tmem + 128 * t, q_desc[t], k_next);
             tc_commit(bar(kSFull + t));
           }
@@ -405,12 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((kSplitP && c == 1) || c == 3) {
           tmem_wait_st();
           tc_fence_before();
-          if (kSplitP) {
-            mbar_arrive(bar((c == 1 ? kPLo : kPHi) + wg));
-          } else {
-            mbar_arrive(bar(kPLo + wg));
-            mbar_arrive(bar(kPHi + wg));
-          }
+          mbar_arrive(bar((c == 1 ? kPLo : kPHi) + wg));
         }
       }
       if (kPackedF32x2) f2_unpack(lsum2, ls0, ls1);
