@@ -71,16 +71,18 @@ constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + barriers + alignmen
 
 // barrier slots
 enum : int {
-  kQFull = 0,      // 2: [0] = Q0 + K(0), [1] = Q1
-  kKVFull = 2,     // kStages: V(j) + K(j+1) landed (stage j % kStages)
-  kKEmpty = 4,     // kStages
-  kVEmpty = 6,     // kStages
-  kSFull = 8,      // 2
-  kPLo = 10,       // 2: P columns for keys [0, 64) written (split publication)
-  kPHi = 12,       // 2: all P columns written
-  kOFull = 14,     // 2
-  kDrain = 16,     // 1
-  kNumBars = 17,
+  kQFull = 0,      // 2: [0] = Q0 + the unit's first K, [1] = Q1
+  kQEmpty = 2,     // 1: the unit's MMAs are done with Q
+  kKVFull = 3,     // kStages: V(j) + K(j+1) landed (stage = global tile % kStages)
+  kKEmpty = 5,     // kStages
+  kVEmpty = 7,     // kStages
+  kSFull = 9,      // 2
+  kPLo = 11,       // 2: P columns for keys [0, 64) written (split publication)
+  kPHi = 13,       // 2: all P columns written
+  kOFull = 15,     // 2: the unit's last PV of query tile t completed
+  kOFree = 17,     // 2: the epilogue has read O_t
+  kDrain = 19,     // 1
+  kNumBars = 20,
 };
 constexpr uint32_t kTmemSlotOff = kSmemBar + 8 * kNumBars;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
@@ -137,16 +139,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kTmemSlotOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
   int* status = p.status;
+  const int num_units = p.num_units;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  Geo geo(p, reinterpret_cast<int*>(smem + kScratchOff));
-  const int n_kv = geo.num_kv_tiles();
-
   if (threadIdx.x == 0) {
     mbar_init(bar(kQFull + 0), 1);
     mbar_init(bar(kQFull + 1), 1);
+    mbar_init(bar(kQEmpty), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kKVFull + s), 1);
       mbar_init(bar(kKEmpty + s), 1);
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kPLo + t), 128);
       mbar_init(bar(kPHi + t), 128);
       mbar_init(bar(kOFull + t), 1);
+      mbar_init(bar(kOFree + t), 128);
     }
     mbar_init(bar(kDrain), 1);
     *abort_flag = 0;
@@ -176,55 +178,83 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Persistent schedule: CTA b processes work units b, b + gridDim.x, ...
+  // Barrier phases run on across units: KV tiles are numbered globally (g)
+  // for the ring, and each role counts the units it has taken part in.
   if (warp == 8) {
     // ------------------------------------------------------------ producer
-    // Order: Q0 + K(0) on Q_FULL[0], Q1 on Q_FULL[1], then per KV tile j the
-    // pair V(j), K(j+1) on one KV_FULL barrier, so the MMA issuer waits once
-    // per KV tile for both operands it needs next.
-    if (lane == 0 && n_kv > 0) {
+    // Per unit: (after the previous unit's MMAs released Q) Q0 + first K on
+    // Q_FULL[0], Q1 on Q_FULL[1]; then per KV tile j the pair V(j), K(j+1) on
+    // one KV_FULL barrier, so the MMA issuer waits once per tile.
+    if (lane == 0) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      mbar_expect_tx(bar(kQFull + 0), 2 * kTileBytes);
-      geo.load_q(&tm_q, 0, sbase + kSmemQ, bar(kQFull + 0), pol_q);
-      geo.load_kv(&tm_k, 0, sbase + kSmemK, bar(kQFull + 0), pol_kv);
-      mbar_expect_tx(bar(kQFull + 1), kTileBytes);
-      geo.load_q(&tm_q, 1, sbase + kSmemQ + kTileBytes, bar(kQFull + 1), pol_q);
-      int jl = -1;  // last KV tile whose V(j) / K(j+1) pair was issued
-      for (int j = 0; j < n_kv; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const bool has_next = j + 1 < n_kv;
-        const int s1 = (j + 1) % kStages;
-        const uint32_t ph1 = ((j + 1) / kStages) & 1;
-        if (!mbar_wait(bar(kVEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) break;
-        if (has_next &&
-            !mbar_wait(bar(kKEmpty + s1), ph1 ^ 1, abort_flag, status, kDevTimeoutLoad))
-          break;
-        mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kTileBytes : kTileBytes);
-        geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kKVFull + s), pol_kv);
-        if (has_next)
-          geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kTileBytes, bar(kKVFull + s), pol_kv);
-        jl = j;
+      uint32_t g = 0;   // global index of the unit's first KV tile
+      int qi = 0;       // units with work issued
+      int last_pair = -1;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+        Geo geo(p, u);
+        const int n = geo.num_kv_tiles();
+        if (n == 0) continue;
+        const int sk = g % kStages;
+        ok = mbar_wait(bar(kQEmpty), (qi & 1) ^ 1, abort_flag, status, kDevTimeoutLoad) &&
+             mbar_wait(bar(kKEmpty + sk), ((g / kStages) & 1) ^ 1, abort_flag, status,
+                       kDevTimeoutLoad);
+        if (!ok) break;
+        mbar_expect_tx(bar(kQFull + 0), 2 * kTileBytes);
+        geo.load_q(&tm_q, 0, sbase + kSmemQ, bar(kQFull + 0), pol_q);
+        geo.load_kv(&tm_k, 0, sbase + kSmemK + sk * kTileBytes, bar(kQFull + 0), pol_kv);
+        mbar_expect_tx(bar(kQFull + 1), kTileBytes);
+        geo.load_q(&tm_q, 1, sbase + kSmemQ + kTileBytes, bar(kQFull + 1), pol_q);
+        for (int j = 0; j < n; ++j) {
+          const uint32_t gj = g + j;
+          const int s = gj % kStages;
+          const uint32_t ph = (gj / kStages) & 1;
+          const bool has_next = j + 1 < n;
+          const int s1 = (gj + 1) % kStages;
+          const uint32_t ph1 = ((gj + 1) / kStages) & 1;
+          if (!mbar_wait(bar(kVEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) {
+            ok = false;
+            break;
+          }
+          if (has_next &&
+              !mbar_wait(bar(kKEmpty + s1), ph1 ^ 1, abort_flag, status, kDevTimeoutLoad)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kTileBytes : kTileBytes);
+          geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kKVFull + s), pol_kv);
+          if (has_next)
+            geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kTileBytes, bar(kKVFull + s),
+                        pol_kv);
+          last_pair = static_cast<int>(gj);
+        }
+        g += n;
+        ++qi;
       }
       if (*abort_flag) {
-        // Drain: wait for the most recent loads into each stage to land so
-        // no TMA write targets this CTA's shared memory after it exits. Only
-        // the last pair per stage can still be pending, so its parity is exact.
-        for (int j = jl; j >= 0 && j > jl - kStages; --j)
-          mbar_wait_drain(bar(kKVFull + j % kStages), (j / kStages) & 1, status);
-        mbar_wait_drain(bar(kQFull + 0), 0, status);
-        mbar_wait_drain(bar(kQFull + 1), 0, status);
+        // Drain: wait for the most recent loads into each stage and into Q
+        // to land so no TMA write targets this CTA's shared memory after it
+        // exits. Only the last load per stage can be pending.
+        for (int gj = last_pair; gj >= 0 && gj > last_pair - kStages; --gj)
+          mbar_wait_drain(bar(kKVFull + gj % kStages), (gj / kStages) & 1, status);
+        if (qi > 0) {
+          mbar_wait_drain(bar(kQFull + 0), (qi - 1) & 1, status);
+          mbar_wait_drain(bar(kQFull + 1), (qi - 1) & 1, status);
+        }
       }
     }
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    // Per KV tile j (all loaded in order): release K(j) (its S MMAs were
-    // issued earlier), then for each query tile t that needs j:
-    //   PV_t(j) after P_t(j) is ready, then S_t(j+1) if t needs j+1.
-    // A query tile that does not need a KV tile skips it entirely (the
-    // neighborhood geometry; the dense one needs every tile).
-    if (lane == 0 && n_kv > 0) {
+    // Per unit and KV tile j: release K(j) (its S MMAs were issued earlier),
+    // wait for V(j) + K(j+1), then for each query tile t that needs j:
+    //   PV_t(j) once P_t(j) is published (and, for the unit's first PV, once
+    //   the previous unit's epilogue has read O_t), then S_t(j+1).
+    // A query tile that does not need a KV tile skips it (neighborhood
+    // geometry; the dense one needs every tile).
+    if (lane == 0) {
       const uint64_t q_desc[2] = {sdesc_sw128(sbase + kSmemQ, 16, 1024),
                                   sdesc_sw128(sbase + kSmemQ + kTileBytes, 16, 1024)};
       static_assert(kStages == 2, "descriptor selection below assumes two stages");
@@ -232,67 +262,99 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t v_desc0 = sdesc_sw128(sbase + kSmemV, kHalfBytes, 1024);
       // stage 1 = stage 0 + kTileBytes in the start-address field
       constexpr uint64_t kStageStep = kTileBytes >> 4;
-      bool ok = mbar_wait(bar(kQFull + 0), 0, abort_flag, status, kDevTimeoutMma) &&
-                mbar_wait(bar(kQFull + 1), 0, abort_flag, status, kDevTimeoutMma);
-      int last[2] = {geo.last_tile(0), geo.last_tile(1)};
-      int pv_count[2] = {0, 0};
-      if (ok) {
+      uint32_t g = 0;
+      int qi = 0;
+      int p_count[2] = {0, 0};  // P publications consumed per query tile
+      int o_units[2] = {0, 0};  // units in which query tile t accumulated O
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+        Geo geo(p, u);
+        const int n = geo.num_kv_tiles();
+        if (n == 0) continue;
+        ok = mbar_wait(bar(kQFull + 0), qi & 1, abort_flag, status, kDevTimeoutMma) &&
+             mbar_wait(bar(kQFull + 1), qi & 1, abort_flag, status, kDevTimeoutMma);
+        if (!ok) break;
+        const int last[2] = {geo.last_tile(0), geo.last_tile(1)};
+        bool first_pv[2] = {true, true};
         tc_fence_after();
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (geo.needs(t, 0)) {
-            issue_qk(tmem + 128 * t, q_desc[t], k_desc0);
+            issue_qk(tmem + 128 * t, q_desc[t], k_desc0 + ((g % kStages) ? kStageStep : 0));
             tc_commit(bar(kSFull + t));
           }
         }
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        const int s1 = (j + 1) % kStages;
-        const bool has_next = j + 1 < n_kv;
-        const uint64_t v_d = v_desc0 + (s ? kStageStep : 0);
-        const uint64_t k_next = k_desc0 + (s1 ? kStageStep : 0);
-        tc_commit(bar(kKEmpty + s));  // every S(j) MMA was issued before this point
-        if (!mbar_wait(bar(kKVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
-        tc_fence_after();
+        // Q is released as soon as the unit's last S MMA has been issued, so
+        // the next unit's Q loads while this unit's last PVs and epilogue run.
+        bool q_released = false;
+        if (n == 1) {
+          tc_commit(bar(kQEmpty));
+          q_released = true;
+        }
+        for (int j = 0; ok && j < n; ++j) {
+          const uint32_t gj = g + j;
+          const int s = gj % kStages;
+          const uint32_t ph = (gj / kStages) & 1;
+          const int s1 = (gj + 1) % kStages;
+          const bool has_next = j + 1 < n;
+          const uint64_t v_d = v_desc0 + (s ? kStageStep : 0);
+          const uint64_t k_next = k_desc0 + (s1 ? kStageStep : 0);
+          tc_commit(bar(kKEmpty + s));  // every S MMA reading K(j) was issued before
+          if (!mbar_wait(bar(kKVFull + s), ph, abort_flag, status, kDevTimeoutMma)) break;
+          tc_fence_after();
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (geo.needs(t, j)) {
-            const uint32_t par = pv_count[t] & 1;
-            if (kSplitP) {
-              if (!mbar_wait(bar(kPLo + t), par, abort_flag, status, kDevTimeoutMma)) {
+          for (int t = 0; t < 2; ++t) {
+            if (geo.needs(t, j)) {
+              if (first_pv[t] && !mbar_wait(bar(kOFree + t), (o_units[t] & 1) ^ 1, abort_flag,
+                                            status, kDevTimeoutMma)) {
+                ok = false;
+                break;
+              }
+              const uint32_t par = p_count[t] & 1;
+              if (kSplitP) {
+                if (!mbar_wait(bar(kPLo + t), par, abort_flag, status, kDevTimeoutMma)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
+              }
+              if (!mbar_wait(bar(kPHi + t), par, abort_flag, status, kDevTimeoutMma)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, pv_count[t] > 0);
+              if (!kSplitP)
+                issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
+              issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 1, true);
+              first_pv[t] = false;
+              ++p_count[t];
+              if (j == last[t]) tc_commit(bar(kOFull + t));
             }
-            if (!mbar_wait(bar(kPHi + t), par, abort_flag, status, kDevTimeoutMma)) {
-              ok = false;
-              break;
+            if (has_next && geo.needs(t, j + 1)) {
+              issue_qk(tmem + 128 * t, q_desc[t], k_next);
+              tc_commit(bar(kSFull + t));
             }
-            tc_fence_after();
-            if (!kSplitP)
-              issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, pv_count[t] > 0);
-            issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 1, true);
-            ++pv_count[t];
-            if (j == last[t]) tc_commit(bar(kOFull + t));
           }
-          if (has_next && geo.needs(t, j + 1)) {
-            issue_qk(tmem + 128 * t, q_desc[t], k_next);
-            tc_commit(bar(kSFull + t));
+          if (!ok) break;
+          if (!q_released && j + 2 == n) {  // S(n-1), the unit's last S, was just issued
+            tc_commit(bar(kQEmpty));
+            q_released = true;
           }
+          tc_commit(bar(kVEmpty + s));
         }
         if (!ok) break;
-        tc_commit(bar(kVEmpty + s));
+        for (int t = 0; t < 2; ++t)
+          if (!first_pv[t]) ++o_units[t];
+        g += n;
+        ++qi;
       }
       // Drain: no MMA may still be running when TMEM is released.
       tc_commit(bar(kDrain));
       mbar_wait_drain(bar(kDrain), 0, status);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ softmax
     const int wg = warp >> 2;    // which query tile
     const int quad = warp & 3;   // TMEM lane quadrant this warp may access
@@ -301,137 +363,147 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t t_s = tmem + wg * 128 + lane_off;
     const uint32_t t_o = tmem + 256 + wg * 128 + lane_off;
     const float scale_log2 = p.scale_log2;
-    geo.softmax_setup(wg, row);
-
-    float m_used = neg_inf();
-    float l_sum = 0.f;
+    int s_count = 0;  // S tiles consumed by this query tile (all units)
+    int o_units = 0;  // units in which this query tile accumulated O
     bool ok = true;
-    int count = 0;  // KV tiles this query tile has processed
-    for (int j = 0; j < n_kv; ++j) {
-      if (!geo.needs(wg, j)) continue;
-      ok = mbar_wait(bar(kSFull + wg), count & 1, abort_flag, status, kDevTimeoutSoftmax);
+    for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+      Geo geo(p, u);
+      const int n_kv = geo.num_kv_tiles();
+      geo.softmax_setup(wg, row);
+      float m_used = neg_inf();
+      float l_sum = 0.f;
+      int count = 0;  // KV tiles this query tile processed in this unit
+      for (int j = 0; j < n_kv; ++j) {
+        if (!geo.needs(wg, j)) continue;
+        ok = mbar_wait(bar(kSFull + wg), s_count & 1, abort_flag, status, kDevTimeoutSoftmax);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sr[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sr[c]);
+        tmem_wait_ld_only();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) pin32(sr[c]);
+
+        geo.mask_scores(j, sr);
+
+        // row max: 3-input max over 128 scores, 4 independent chains
+        float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            mx0 = fmax3(mx0, __uint_as_float(sr[c][i + 0]), __uint_as_float(sr[c][i + 1]));
+            mx1 = fmax3(mx1, __uint_as_float(sr[c][i + 2]), __uint_as_float(sr[c][i + 3]));
+            mx2 = fmax3(mx2, __uint_as_float(sr[c][i + 4]), __uint_as_float(sr[c][i + 5]));
+            mx3 = fmax3(mx3, __uint_as_float(sr[c][i + 6]), __uint_as_float(sr[c][i + 7]));
+          }
+        }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale_log2;
+        const float m_new = fmaxf(m_used, mx);
+        const bool need = m_new > m_used + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) alpha = ex2_approx(m_used - m_new);  // 0 when m_used = -inf
+        if (count > 0 && __any_sync(0xffffffffu, need)) {
+          // O is complete up to this query tile's previous KV tile: S(j) was
+          // issued after that PV and its commit tracks every earlier MMA.
+          // Rescale this warp's 32 rows of O.
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t orr[32];
+            tmem_ld32(t_o + c * 32, orr);
+            tmem_wait_ld(orr);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+            tmem_st32(t_o + c * 32, orr);
+          }
+        }
+        if (need) {
+          l_sum *= alpha;
+          m_used = m_new;
+        }
+        const float neg_m = (m_used == neg_inf()) ? 0.f : -m_used;
+        // p = 2^(s * scale_log2 - m); optionally one pair in kPolyEvery goes
+        // through the FMA-pipe polynomial instead of MUFU ex2.
+        const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+        const uint64_t negm2 = f2_pack(neg_m, neg_m);
+        uint64_t lsum2 = f2_pack(0.f, 0.f);
+        float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float x0, x1, e0, e1;
+            if (kPackedF32x2) {
+              const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c][2 * i]),
+                                                 __uint_as_float(sr[c][2 * i + 1])),
+                                         scale2, negm2);
+              f2_unpack(x2, x0, x1);
+            } else {
+              x0 = fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m);
+              x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m);
+            }
+            if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
+              e0 = exp2_poly(x0);
+              e1 = exp2_poly(x1);
+            } else {
+              e0 = ex2_approx(x0);
+              e1 = ex2_approx(x1);
+            }
+            if (kPackedF32x2) {
+              lsum2 = f2_add(lsum2, f2_pack(e0, e1));
+            } else {
+              ls0 += e0;
+              ls1 += e1;
+            }
+            pk[i] = pack_bf16x2(e0, e1);
+          }
+          tmem_st16(t_s + c * 16, pk);
+          if ((kSplitP && c == 1) || c == 3) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar((c == 1 ? kPLo : kPHi) + wg));
+          }
+        }
+        if (kPackedF32x2) f2_unpack(lsum2, ls0, ls1);
+        l_sum += ls0 + ls1;
+        ++s_count;
+        ++count;
+      }
+      if (!ok) break;
+      if (count == 0) {
+        geo.store_zero_row(wg, row);
+        continue;
+      }
+      ok = mbar_wait(bar(kOFull + wg), o_units & 1, abort_flag, status, kDevTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sr[c]);
-      tmem_wait_ld_only();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) pin32(sr[c]);
-
-      geo.mask_scores(j, sr);
-
-      // row max: 3-input max over 128 scores, 4 independent chains
-      float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
+      const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      uint32_t pk[4][16];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        uint32_t orr[32];
+        tmem_ld32(t_o + c * 32, orr);
+        tmem_wait_ld(orr);
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          mx0 = fmax3(mx0, __uint_as_float(sr[c][i + 0]), __uint_as_float(sr[c][i + 1]));
-          mx1 = fmax3(mx1, __uint_as_float(sr[c][i + 2]), __uint_as_float(sr[c][i + 3]));
-          mx2 = fmax3(mx2, __uint_as_float(sr[c][i + 4]), __uint_as_float(sr[c][i + 5]));
-          mx3 = fmax3(mx3, __uint_as_float(sr[c][i + 6]), __uint_as_float(sr[c][i + 7]));
-        }
+        for (int i = 0; i < 16; ++i)
+          pk[c][i] = pack_bf16x2(__uint_as_float(orr[2 * i]) * inv_l,
+                                 __uint_as_float(orr[2 * i + 1]) * inv_l);
       }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale_log2;
-      const float m_new = fmaxf(m_used, mx);
-      const bool need = m_new > m_used + kRescaleThreshold;
-      float alpha = 1.f;
-      if (need) alpha = ex2_approx(m_used - m_new);  // 0 when m_used = -inf
-      if (count > 0 && __any_sync(0xffffffffu, need)) {
-        // O is complete up to this query tile's previous KV tile: S(j) was
-        // issued after that PV and its commit tracks every earlier MMA.
-        // Rescale this warp's 32 rows of O.
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t orr[32];
-          tmem_ld32(t_o + c * 32, orr);
-          tmem_wait_ld(orr);
+      // O_t has been read: the next unit's first PV may overwrite it.
+      tc_fence_before();
+      mbar_arrive(bar(kOFree + wg));
+      ++o_units;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-          tmem_st32(t_o + c * 32, orr);
-        }
-      }
-      if (need) {
-        l_sum *= alpha;
-        m_used = m_new;
-      }
-      const float neg_m = (m_used == neg_inf()) ? 0.f : -m_used;
-      // p = 2^(s * scale_log2 - m): packed f32x2 FMA for the argument; one
-      // pair in four goes through the FMA-pipe polynomial, the rest through
-      // MUFU ex2. P is published in two halves (keys [0,64), [64,128)).
-      const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
-      const uint64_t negm2 = f2_pack(neg_m, neg_m);
-      uint64_t lsum2 = f2_pack(0.f, 0.f);
-      float ls0 = 0.f, ls1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x0, x1, e0, e1;
-          if (kPackedF32x2) {
-            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c][2 * i]),
-                                               __uint_as_float(sr[c][2 * i + 1])),
-                                       scale2, negm2);
-            f2_unpack(x2, x0, x1);
-          } else {
-            x0 = fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m);
-            x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m);
-          }
-          if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
-            e0 = exp2_poly(x0);
-            e1 = exp2_poly(x1);
-          } else {
-            e0 = ex2_approx(x0);
-            e1 = ex2_approx(x1);
-          }
-          if (kPackedF32x2) {
-            lsum2 = f2_add(lsum2, f2_pack(e0, e1));
-          } else {
-            ls0 += e0;
-            ls1 += e1;
-          }
-          pk[i] = pack_bf16x2(e0, e1);
-        }
-        tmem_st16(t_s + c * 16, pk);
-        if ((kSplitP && c == 1) || c == 3) {
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(bar((c == 1 ? kPLo : kPHi) + wg));
-        }
-      }
-      if (kPackedF32x2) f2_unpack(lsum2, ls0, ls1);
-      l_sum += ls0 + ls1;
-      ++count;
-    }
-
-    if (ok && count == 0) {
-      geo.store_zero_row(wg, row);
-    } else if (ok) {
-      ok = mbar_wait(bar(kOFull + wg), 0, abort_flag, status, kDevTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t orr[32];
-          tmem_ld32(t_o + c * 32, orr);
-          tmem_wait_ld(orr);
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16x2(__uint_as_float(orr[2 * i]) * inv_l,
-                                __uint_as_float(orr[2 * i + 1]) * inv_l);
-          geo.store_row_chunk(wg, row, c, pk);
-        }
-        // natural-log LSE of the row's scaled logits
-        const float lse = l_sum > 0.f ? (m_used + __log2f(l_sum)) * 0.69314718055994531f
-                                      : neg_inf();
-        geo.store_lse(wg, row, lse);
-      }
+      for (int c = 0; c < 4; ++c) geo.store_row_chunk(wg, row, c, pk[c]);
+      // natural-log LSE of the row's scaled logits
+      const float lse = l_sum > 0.f ? (m_used + __log2f(l_sum)) * 0.69314718055994531f
+                                    : neg_inf();
+      geo.store_lse(wg, row, lse);
     }
   }
 
@@ -454,6 +526,8 @@ struct DenseParams {
   const int* kv_len;           // optional [B]
   int* status;
   int B, Sq, Sk, H, Hkv;
+  int num_qblocks;             // ceil(Sq / 256)
+  int num_units;               // num_qblocks * H * B
   float scale_log2;
 };
 
@@ -463,10 +537,14 @@ struct DenseGeo {
   int b, h, hk, q0, kv_valid;
   int row_global;
 
-  __device__ DenseGeo(const DenseParams& prm, int*) : p(prm) {
-    q0 = blockIdx.x * (2 * kBlockM);
-    h = blockIdx.y;
-    b = blockIdx.z;
+  // Work unit u = (query block, head, batch), query block fastest so that
+  // the CTAs running at the same time share a head's K/V through L2.
+  __device__ DenseGeo(const DenseParams& prm, int unit) : p(prm) {
+    const int qb = unit % p.num_qblocks;
+    const int rest = unit / p.num_qblocks;
+    q0 = qb * (2 * kBlockM);
+    h = rest % p.H;
+    b = rest / p.H;
     hk = h / (p.H / p.Hkv);
     int kv = p.Sk;
     if (p.kv_len != nullptr) kv = min(max(p.kv_len[b], 0), p.Sk);
@@ -552,6 +630,8 @@ struct NaParams {
   int qbox[3];             // query box (t, h, w), product 128
   int pair_axis;           // 0 = t, 1 = h, 2 = w
   int regions[3];          // CTA regions per axis
+  int num_regions;         // regions[0] * regions[1] * regions[2]
+  int num_units;           // num_regions * NH * B
   float scale_log2;
   int round_logits;        // round q.k to bf16 before the softmax (vidax's einsum output dtype)
 };
@@ -587,16 +667,18 @@ struct NaGeo {
   int ws[3];              // window starts
   bool row_valid;
 
-  __device__ NaGeo(const NaParams& prm, int*) : p(prm) {
-    head = blockIdx.y;
-    b = blockIdx.z;
+  // Work unit u = (region, head, batch), region fastest.
+  __device__ NaGeo(const NaParams& prm, int unit) : p(prm) {
+    const int rest = unit / p.num_regions;
+    head = rest % p.NH;
+    b = rest / p.NH;
     head_kv = head / (p.NH / p.NHkv);
     lim[0] = p.T;
     lim[1] = p.H;
     lim[2] = p.W;
     const int ksz[3] = {p.kt, p.kh, p.kw};
     int reg[3];
-    int r = blockIdx.x;
+    int r = unit % p.num_regions;
     reg[2] = r % p.regions[2];
     r /= p.regions[2];
     reg[1] = r % p.regions[1];

@@ -133,6 +133,17 @@ int bshd_tmap(CUtensorMap* tm, const char* name, const void* ptr, const int64_t*
   return make_tmap(tm, ptr, 4, dims, strides, box);
 }
 
+int num_sms(int dev, int* out) {
+  static int cache[kMaxDevices] = {};
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (cache[dev] == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+  }
+  *out = cache[dev];
+  return VX_OK;
+}
+
 int prepare_kernel(const void* fn, int dev, size_t smem) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_attr_set.count({fn, dev}) == 0) {
@@ -228,10 +239,16 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
   p.H = a->heads_q;
   p.Hkv = a->heads_kv;
   p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.num_qblocks = (a->seq_q + 2 * kBlockM - 1) / (2 * kBlockM);
+  const long long units = static_cast<long long>(p.num_qblocks) * a->heads_q * a->batch;
+  if (units > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "too many work units");
+  p.num_units = static_cast<int>(units);
 
   auto kern = attn_fwd_kernel<DenseGeo>;
   if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
-  dim3 grid((a->seq_q + 2 * kBlockM - 1) / (2 * kBlockM), a->heads_q, a->batch);
+  int sms = 0;
+  if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
+  dim3 grid(static_cast<unsigned>(std::min<long long>(units, sms)));
   kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
@@ -487,14 +504,19 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
     p.regions[i] = (lim[i] + rsz - 1) / rsz;
     n_regions *= p.regions[i];
   }
-  if (n_regions > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "grid too large");
+  const long long units = n_regions * a->heads * a->batch;
+  if (units > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "grid too large");
+  p.num_regions = static_cast<int>(n_regions);
+  p.num_units = static_cast<int>(units);
   p.pair_axis = ch.pair;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.round_logits = a->round_logits ? 1 : 0;
 
   auto kern = attn_fwd_kernel<NaGeoDefault>;
   if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
-  dim3 grid(static_cast<unsigned>(n_regions), a->heads, a->batch);
+  int sms = 0;
+  if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
+  dim3 grid(static_cast<unsigned>(std::min<long long>(units, sms)));
   kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "na3d_fwd launch");
