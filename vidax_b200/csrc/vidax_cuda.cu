@@ -514,9 +514,9 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
 
   auto kern = attn_fwd_kernel<NaGeoDefault>;
   if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
-  int sms = 0;
-  if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
-  dim3 grid(static_cast<unsigned>(std::min<long long>(units, sms)));
+  // One work unit per CTA: neighborhood units are short (tens of KV tiles),
+  // and a fresh CTA per unit measured faster than the persistent hand-off.
+  dim3 grid(static_cast<unsigned>(units));
   kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "na3d_fwd launch");
