@@ -135,6 +135,16 @@ int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);
  * (diffusion_vae.py:152-164). Returns VX_EINVAL for length/kernel < 1. */
 int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out);
 
+/* ----------------------------------------------------------------------
+ * Strided row copy (host <-> device or device <-> device), stream-ordered:
+ * `rows` rows of `row_bytes` bytes from src (pitch src_pitch) to dst (pitch
+ * dst_pitch). Used by the host-buffer attention path to move one head group
+ * of a BSHD tensor (a 2-D strided slab) while other groups compute; host
+ * memory must be page-locked for the copy to overlap.
+ */
+int vx_memcpy_rows_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                         int64_t row_bytes, int64_t rows, vx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

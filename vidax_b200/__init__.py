@@ -18,6 +18,7 @@ from .attention import (  # noqa: F401
     flash_attention,
     local_attention,
 )
+from .hostio import attention_from_host  # noqa: F401
 from .neighborhood import na3d_flops, neighborhood_attention_3d  # noqa: F401
 from .ulysses import (  # noqa: F401
     axis_index,

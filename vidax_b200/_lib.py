@@ -27,6 +27,11 @@ EXPORTED_SYMBOLS = (
     "vx_last_error",
     "vx_device_status",
     "vx_attn_fwd",
+    "vx_na3d_fwd",
+    "vx_na3d_window_start",
+    "vx_ulysses_pack",
+    "vx_ulysses_unpack",
+    "vx_memcpy_rows_async",
 )
 
 
@@ -98,6 +103,10 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.vx_device_status.restype = ctypes.c_int
         lib.vx_attn_fwd.argtypes = [ctypes.POINTER(AttnArgs), ctypes.c_void_p]
         lib.vx_attn_fwd.restype = ctypes.c_int
+        lib.vx_memcpy_rows_async.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_void_p]
+        lib.vx_memcpy_rows_async.restype = ctypes.c_int
         _lib = lib
         return lib
 

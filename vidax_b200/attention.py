@@ -140,6 +140,9 @@ def local_attention(
     device's kernel, no cross-device communication. Default scale D^-0.5."""
     head_dim = q.shape[-1]
     sm_scale = head_dim ** -0.5 if scale is None else scale
+    if q.device.type == "cpu":
+        from .hostio import attention_from_host
+        return attention_from_host(q, k, v, sm_scale)
     return flash_attention(q, k, v, sm_scale)
 
 
@@ -153,7 +156,9 @@ def dot_product_attention(
     """Full (non-causal) attention (attention.py:467-533).
 
     q, k, v: (B, S, num_heads, head_dim); k/v may have another sequence
-    length (cross-attention). `scale` defaults to head_dim ** -0.5.
+    length (cross-attention). `scale` defaults to head_dim ** -0.5. CUDA
+    tensors run in place; host (pinned) tensors take the pipelined
+    host-buffer path and return a host tensor.
     `bias` / `mask` are accepted only in their key-padding forms ((B,1,1,Sk)
     0/-inf bias or boolean valid-prefix mask), which become per-batch key
     lengths for the kernel; dense biases and general masks raise
@@ -172,6 +177,10 @@ def dot_product_attention(
         kv_len = _key_lengths_from_mask(mask, B, Sk)
     elif bias is not None:
         kv_len = _key_lengths_from_bias(bias, B, Sk)
+    if q.device.type == "cpu":
+        # host tensors: transfers pipelined against the kernel (vidax_b200.hostio)
+        from .hostio import attention_from_host
+        return attention_from_host(q, k, v, sm_scale, kv_len=kv_len)
     return flash_attention(q, k, v, sm_scale, kv_len=kv_len)
 
 

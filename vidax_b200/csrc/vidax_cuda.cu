@@ -524,3 +524,19 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
 }
 
 }  // extern "C"
+
+extern "C" int vx_memcpy_rows_async(void* dst, int64_t dst_pitch, const void* src,
+                                    int64_t src_pitch, int64_t row_bytes, int64_t rows,
+                                    vx_stream_t stream) {
+  if (rows == 0 || row_bytes == 0) return VX_OK;
+  if (dst == nullptr || src == nullptr) return fail(VX_EINVAL, "NULL pointer");
+  if (row_bytes < 0 || rows < 0 || dst_pitch < row_bytes || src_pitch < row_bytes)
+    return fail(VX_EINVAL, "bad copy geometry (row_bytes %lld, pitches %lld / %lld)",
+                (long long)row_bytes, (long long)dst_pitch, (long long)src_pitch);
+  cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_pitch), src,
+                                    static_cast<size_t>(src_pitch), static_cast<size_t>(row_bytes),
+                                    static_cast<size_t>(rows), cudaMemcpyDefault,
+                                    reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
+  return VX_OK;
+}
