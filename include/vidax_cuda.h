@@ -70,7 +70,15 @@ typedef struct vx_attn_args {
   float scale;             /* softmax scale, > 0 */
   const int32_t* kv_len;   /* optional device int32[B]; NULL = all seq_k keys valid */
   float* lse;              /* optional device fp32 (B, Hq, Sq): natural-log sum-exp */
+  int32_t schedule;        /* VX_SCHED_STATIC (default) or VX_SCHED_DYNAMIC */
 } vx_attn_args;
+
+/* Work distribution of vx_attn_fwd: STATIC = one CTA per SM, each taking a
+ * fixed share of the (query block, head, batch) units -- best when the kernel
+ * has the GPU to itself; DYNAMIC = CTAs take over not-yet-launched work at run
+ * time (hardware cluster launch control) -- best when other kernels (e.g.
+ * collectives) run concurrently and hold some SMs. */
+enum { VX_SCHED_STATIC = 0, VX_SCHED_DYNAMIC = 1 };
 
 int vx_attn_fwd(const vx_attn_args* args, vx_stream_t stream);
 
@@ -92,6 +100,13 @@ typedef struct vx_head_slab_args {
   void* dst[3];
   int64_t stride[3][2];  /* strided side, element strides of (seq, heads); d stride 1 */
   int32_t seq, heads, head_dim, groups;
+  /* Optional sub-group selection (all 0 = whole groups): packed head i of
+   * group g is strided head head_offset + g * group_stride + i for
+   * i < slab_heads; heads with i >= group_valid or index >= `heads` are
+   * zero (pack) / skipped (unpack). Lets one all-to-all move a sub-group of
+   * every rank's head group, so transfers can be pipelined against the
+   * attention kernel. */
+  int32_t slab_heads, group_stride, head_offset, group_valid;
 } vx_head_slab_args;
 
 /* strided (seq, heads, D) rows -> contiguous (groups, seq, hg, D) */

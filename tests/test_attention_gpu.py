@@ -184,3 +184,19 @@ def test_host_buffer_path_matches_oracle(B, S, Sk, H, Hkv, hpg):
     out2 = vx.dot_product_attention(hq, hk, hv)
     torch.cuda.synchronize()
     assert torch.equal(out, out2)
+
+
+@pytest.mark.gpu
+def test_dynamic_schedule_matches_static():
+    """The run-time (cluster launch control) schedule computes every work
+    unit exactly as the static one: identical bits, and oracle parity."""
+    import vidax_b200 as vx
+    q, k, v = seeded_qkv((2, 1500, 6, 128), 71)
+    tq, tk, tv = _dev(q), _dev(k), _dev(v)
+    o_static = vx.flash_attention(tq, tk, tv, 128 ** -0.5)
+    o_dyn = vx.flash_attention(tq, tk, tv, 128 ** -0.5, dynamic_schedule=True)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    assert torch.equal(o_static, o_dyn)
+    mx, mean = compare(_host(o_dyn), sdpa(q, k, v))
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

@@ -84,3 +84,28 @@ def test_ulysses_two_gpus_nccl():
     res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "ULYSSES OK" in res.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,P,hs", [(40, 8, 1), (40, 2, 4), (12, 8, 1), (10, 4, 2), (6, 4, 1)])
+def test_sub_group_pack_unpack_bit_exact(H, P, hs):
+    """Slices of every rank's head group (the pipelined exchange): packed
+    layout against direct indexing, and unpacking all slices restores x."""
+    from vidax_b200.ulysses import pack_heads, unpack_heads
+    S_loc = 96
+    x = torch.randn((S_loc, H, 128), device="cuda").bfloat16()
+    Hg = -(-H // P)
+    back = torch.zeros_like(x)
+    for j in range(-(-Hg // hs)):
+        valid = min(hs, Hg - j * hs)
+        sub = (hs, Hg, j * hs, valid)
+        packed, = pack_heads([x], P, sub=sub)
+        ref = torch.zeros((P, S_loc, hs, 128), dtype=x.dtype, device="cuda")
+        for g in range(P):
+            for i in range(valid):
+                h = g * Hg + j * hs + i
+                if h < H:
+                    ref[g, :, i] = x[:, h]
+        assert torch.equal(packed, ref)
+        unpack_heads([packed], [back], H, sub=sub)
+    assert torch.equal(back, x)

@@ -68,7 +68,11 @@ class AttnArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("kv_len", ctypes.c_void_p),
         ("lse", ctypes.c_void_p),
+        ("schedule", ctypes.c_int32),
     ]
+
+
+VX_SCHED_STATIC, VX_SCHED_DYNAMIC = 0, 1
 
 
 _lock = threading.Lock()

@@ -52,12 +52,15 @@ def flash_attention(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
     kv_len: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
     return_lse: bool = False, stream: Optional[torch.cuda.Stream] = None,
+    dynamic_schedule: bool = False,
 ):
     """Runs the sm_100a attention kernel: softmax(scale * q k^T) v, per (b, h).
 
     q: (B, Sq, Hq, D), k/v: (B, Sk, Hkv, D) with Hq % Hkv == 0, bf16 on one
     CUDA device. `kv_len` (int32 [B], device) hides keys at index >= kv_len[b]
     -- the key-side SegmentIds padding mask of attention.py:272-278.
+    `dynamic_schedule` distributes work at run time (for launches that share
+    the GPU with concurrent kernels such as NCCL collectives).
     Returns o (B, Sq, Hq, D) bf16 [and lse (B, Hq, Sq) fp32].
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -90,6 +93,7 @@ def flash_attention(
     a.scale = float(scale)
     a.kv_len = kv_len.data_ptr() if kv_len is not None else None
     a.lse = lse.data_ptr() if lse is not None else None
+    a.schedule = _lib.VX_SCHED_DYNAMIC if dynamic_schedule else _lib.VX_SCHED_STATIC
     lib = _lib.load()
     with torch.cuda.device(q.device):
         s = stream if stream is not None else torch.cuda.current_stream(q.device)

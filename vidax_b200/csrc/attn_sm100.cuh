@@ -82,11 +82,17 @@ enum : int {
   kOFull = 15,     // 2: the unit's last PV of query tile t completed
   kOFree = 17,     // 2: the epilogue has read O_t
   kDrain = 19,     // 1
-  kNumBars = 20,
+  kUnitFull = 20,  // 2: unit ring slot written by the scheduler
+  kUnitEmpty = 22, // 2: unit ring slot read by the MMA issuer and all softmax threads
+  kClc = 24,       // 1: cluster-launch-control response landed
+  kNumBars = 25,
 };
 constexpr uint32_t kTmemSlotOff = kSmemBar + 8 * kNumBars;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
-constexpr uint32_t kScratchOff = kAbortOff + 4;  // 16 ints of per-CTA scratch
+constexpr uint32_t kUnitRingOff = kAbortOff + 4;                   // 2 ints
+constexpr uint32_t kClcRespOff = (kUnitRingOff + 8 + 15) & ~15u;   // 16 bytes, 16-aligned
+static_assert(kClcRespOff + 16 <= kSmemBar + 256, "control block exceeds its reservation");
+constexpr int kUnitConsumers = 1 + 256;  // MMA issuer + every softmax thread
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false, false);  // Q K^T: both K-major
 constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, false, true);   // P V : V is N-major
@@ -125,7 +131,14 @@ __device__ __forceinline__ void issue_pv_half(uint32_t tmem_o, uint32_t tmem_p, 
 
 __device__ __forceinline__ void pin32(uint32_t (&r)[32]) { asm volatile("" : VX_RW32(r)); }
 
-template <class Geo>
+// Work scheduling of attn_fwd_kernel (template parameter kSched).
+enum : int {
+  kSchedSingle = 0,  // grid = units, each CTA runs exactly its own unit
+  kSchedStride = 1,  // grid = min(units, SMs), CTA b runs units b, b + grid, ...
+  kSchedSteal = 2,   // grid = units, running CTAs take over unlaunched ones (CLC)
+};
+
+template <class Geo, int kSched>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
@@ -139,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kTmemSlotOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
   int* status = p.status;
-  const int num_units = p.num_units;
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(smem + kUnitRingOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -161,6 +174,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kOFree + t), 128);
     }
     mbar_init(bar(kDrain), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(kUnitFull + i), 1);
+      mbar_init(bar(kUnitEmpty + i), kUnitConsumers);
+    }
+    mbar_init(bar(kClc), 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -178,9 +196,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Persistent schedule: CTA b processes work units b, b + gridDim.x, ...
-  // Barrier phases run on across units: KV tiles are numbered globally (g)
-  // for the ring, and each role counts the units it has taken part in.
+  // Schedule: each CTA processes its own unit (blockIdx.x) first. Then, with
+  // kSchedStride, units blockIdx.x + gridDim.x, ...; with kSchedSteal it asks
+  // the hardware (cluster launch control) to cancel a CTA that has not
+  // launched yet and processes that CTA's unit instead, until none is left --
+  // a persistent, dynamically balanced schedule that adapts when other
+  // kernels (e.g. NCCL's) hold some SMs. The producer thread is the
+  // scheduler: it publishes the unit sequence (ending with -1) through a
+  // two-slot ring in shared memory that the MMA issuer and the softmax
+  // threads read. Barrier phases run on across units: KV tiles
+  // are numbered globally (g) for the ring, and each role counts the units
+  // it has taken part in.
+  auto next_unit = [&](int k, int code, int& u) -> bool {
+    // consumer side of the unit ring: k-th published unit
+    if (!mbar_wait(bar(kUnitFull + (k & 1)), (k >> 1) & 1, abort_flag, status, code)) return false;
+    u = unit_ring[k & 1];
+    mbar_arrive(bar(kUnitEmpty + (k & 1)));
+    return true;
+  };
   if (warp == 8) {
     // ------------------------------------------------------------ producer
     // Per unit: (after the previous unit's MMAs released Q) Q0 + first K on
@@ -189,49 +222,82 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
+      const uint32_t clc_resp = sbase + kClcRespOff;
       uint32_t g = 0;   // global index of the unit's first KV tile
       int qi = 0;       // units with work issued
       int last_pair = -1;
+      int clc_issued = 0, clc_done = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+      auto publish = [&](int k, int u) -> bool {
+        if (!mbar_wait(bar(kUnitEmpty + (k & 1)), ((k >> 1) & 1) ^ 1, abort_flag, status,
+                       kDevTimeoutLoad))
+          return false;
+        unit_ring[k & 1] = u;
+        mbar_arrive(bar(kUnitFull + (k & 1)));
+        return true;
+      };
+      int u = blockIdx.x;
+      ok = publish(0, u);
+      for (int k = 1; ok && u >= 0; ++k) {
         Geo geo(p, u);
         const int n = geo.num_kv_tiles();
-        if (n == 0) continue;
-        const int sk = g % kStages;
-        ok = mbar_wait(bar(kQEmpty), (qi & 1) ^ 1, abort_flag, status, kDevTimeoutLoad) &&
-             mbar_wait(bar(kKEmpty + sk), ((g / kStages) & 1) ^ 1, abort_flag, status,
-                       kDevTimeoutLoad);
-        if (!ok) break;
-        mbar_expect_tx(bar(kQFull + 0), 2 * kTileBytes);
-        geo.load_q(&tm_q, 0, sbase + kSmemQ, bar(kQFull + 0), pol_q);
-        geo.load_kv(&tm_k, 0, sbase + kSmemK + sk * kTileBytes, bar(kQFull + 0), pol_kv);
-        mbar_expect_tx(bar(kQFull + 1), kTileBytes);
-        geo.load_q(&tm_q, 1, sbase + kSmemQ + kTileBytes, bar(kQFull + 1), pol_q);
-        for (int j = 0; j < n; ++j) {
-          const uint32_t gj = g + j;
-          const int s = gj % kStages;
-          const uint32_t ph = (gj / kStages) & 1;
-          const bool has_next = j + 1 < n;
-          const int s1 = (gj + 1) % kStages;
-          const uint32_t ph1 = ((gj + 1) / kStages) & 1;
-          if (!mbar_wait(bar(kVEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) {
-            ok = false;
-            break;
-          }
-          if (has_next &&
-              !mbar_wait(bar(kKEmpty + s1), ph1 ^ 1, abort_flag, status, kDevTimeoutLoad)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kTileBytes : kTileBytes);
-          geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kKVFull + s), pol_kv);
-          if (has_next)
-            geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kTileBytes, bar(kKVFull + s),
-                        pol_kv);
-          last_pair = static_cast<int>(gj);
+        if (kSched == kSchedSteal) {
+          // request the next unit now; the answer is needed only after this
+          // unit's loads are issued
+          mbar_expect_tx(bar(kClc), 16);
+          clc_try_cancel(clc_resp, bar(kClc));
+          ++clc_issued;
         }
-        g += n;
-        ++qi;
+        if (n > 0) {
+          const int sk = g % kStages;
+          ok = mbar_wait(bar(kQEmpty), (qi & 1) ^ 1, abort_flag, status, kDevTimeoutLoad) &&
+               mbar_wait(bar(kKEmpty + sk), ((g / kStages) & 1) ^ 1, abort_flag, status,
+                         kDevTimeoutLoad);
+          if (!ok) break;
+          mbar_expect_tx(bar(kQFull + 0), 2 * kTileBytes);
+          geo.load_q(&tm_q, 0, sbase + kSmemQ, bar(kQFull + 0), pol_q);
+          geo.load_kv(&tm_k, 0, sbase + kSmemK + sk * kTileBytes, bar(kQFull + 0), pol_kv);
+          mbar_expect_tx(bar(kQFull + 1), kTileBytes);
+          geo.load_q(&tm_q, 1, sbase + kSmemQ + kTileBytes, bar(kQFull + 1), pol_q);
+          for (int j = 0; j < n; ++j) {
+            const uint32_t gj = g + j;
+            const int s = gj % kStages;
+            const uint32_t ph = (gj / kStages) & 1;
+            const bool has_next = j + 1 < n;
+            const int s1 = (gj + 1) % kStages;
+            const uint32_t ph1 = ((gj + 1) / kStages) & 1;
+            if (!mbar_wait(bar(kVEmpty + s), ph ^ 1, abort_flag, status, kDevTimeoutLoad)) {
+              ok = false;
+              break;
+            }
+            if (has_next &&
+                !mbar_wait(bar(kKEmpty + s1), ph1 ^ 1, abort_flag, status, kDevTimeoutLoad)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kTileBytes : kTileBytes);
+            geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kKVFull + s), pol_kv);
+            if (has_next)
+              geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kTileBytes, bar(kKVFull + s),
+                          pol_kv);
+            last_pair = static_cast<int>(gj);
+          }
+          if (!ok) break;
+          g += n;
+          ++qi;
+        }
+        int nu = -1;
+        if (kSched == kSchedStride && u + static_cast<int>(gridDim.x) < p.num_units)
+          nu = u + static_cast<int>(gridDim.x);
+        if (kSched == kSchedSteal) {
+          if (!mbar_wait(bar(kClc), clc_done & 1, abort_flag, status, kDevTimeoutLoad)) break;
+          ++clc_done;
+          int x;
+          if (clc_query(clc_resp, x)) nu = x;
+          fence_proxy_async_smem();  // the read precedes the next async response write
+        }
+        ok = publish(k, nu);
+        u = nu;
       }
       if (*abort_flag) {
         // Drain: wait for the most recent loads into each stage and into Q
@@ -243,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait_drain(bar(kQFull + 0), (qi - 1) & 1, status);
           mbar_wait_drain(bar(kQFull + 1), (qi - 1) & 1, status);
         }
+        if (clc_issued > clc_done) mbar_wait_drain(bar(kClc), clc_done & 1, status);
       }
     }
     __syncwarp();
@@ -267,7 +334,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int p_count[2] = {0, 0};  // P publications consumed per query tile
       int o_units[2] = {0, 0};  // units in which query tile t accumulated O
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+      for (int k = 0; ok; ++k) {
+        int u;
+        if (!next_unit(k, kDevTimeoutMma, u) || u < 0) break;
         Geo geo(p, u);
         const int n = geo.num_kv_tiles();
         if (n == 0) continue;
@@ -366,7 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int s_count = 0;  // S tiles consumed by this query tile (all units)
     int o_units = 0;  // units in which this query tile accumulated O
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < num_units; u += gridDim.x) {
+    for (int k = 0; ok; ++k) {
+      int u;
+      ok = next_unit(k, kDevTimeoutSoftmax, u);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || u < 0) break;
       Geo geo(p, u);
       const int n_kv = geo.num_kv_tiles();
       geo.softmax_setup(wg, row);

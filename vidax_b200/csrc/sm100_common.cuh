@@ -133,6 +133,35 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+// ---------------------------------------------------------------- cluster launch control
+// Asks the hardware to cancel one not-yet-launched CTA of this grid; the
+// 16-byte response lands in shared memory (`resp`, 16-byte aligned) and
+// completes as transaction bytes on `bar`.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 "
+      "[%0], [%1];" ::"r"(resp),
+      "r"(bar)
+      : "memory");
+}
+// Decodes a try_cancel response: true and the canceled CTA's x index when a
+// CTA was canceled (its work now belongs to the caller), false when none was
+// left to cancel.
+__device__ __forceinline__ bool clc_query(uint32_t resp, int& ctaid_x) {
+  uint32_t x = 0, valid = 0;
+  asm volatile(
+      "{\n\t.reg .pred p1;\n\t.reg .b128 res;\n\t"
+      "ld.shared.b128 res, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p1, res;\n\t"
+      "selp.u32 %1, 1, 0, p1;\n\t"
+      "@p1 clusterlaunchcontrol.query_cancel.get_first_ctaid.v4.b32.b128 {%0, _, _, _}, res;\n\t}\n"
+      : "+r"(x), "=r"(valid)
+      : "r"(resp)
+      : "memory");
+  ctaid_x = static_cast<int>(x);
+  return valid != 0;
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),

@@ -10,7 +10,9 @@
 //           -> dst (G, S_loc, Hg, D) contiguous, h = g*Hg + hg
 //
 // where Hg = ceil(H / G); heads h >= H (padding when H % G != 0) are written
-// as zeros. The receiving rank then holds (G_src, S_loc, Hg, D) = (S, Hg, D)
+// as zeros. A sub-group form packs heads head_offset + g*group_stride + i,
+// i < Hg, of each group (one slice of every rank's head group), so the
+// exchange can be split into pipelined pieces. The receiving rank then holds (G_src, S_loc, Hg, D) = (S, Hg, D)
 // in natural token order, which the attention kernel reads directly.
 //
 // The inverse (heads->tokens, attention.py:388) unpacks the received
@@ -37,6 +39,9 @@ struct PackParams {
   int hg;        // heads per group on the packed side
   int groups;    // G
   int vpd_log2;  // log2(D / 8): 16-byte vectors per head row
+  int group_stride;  // strided-side heads between consecutive groups
+  int head_offset;   // strided head of group 0's first packed head
+  int group_valid;   // packed heads per group that map to real heads
 };
 
 // grid = (x: chunks of the (s, hg, d) plane of one group, y: group, z: tensor).
@@ -56,14 +61,16 @@ __global__ void __launch_bounds__(256) head_slab_kernel(const __grid_constant__ 
        idx += static_cast<long long>(gridDim.x) * 256) {
     const int s = static_cast<int>(idx / row_vecs);
     const int c = static_cast<int>(idx - static_cast<long long>(s) * row_vecs);
-    const int h = g * p.hg + (c >> p.vpd_log2);
+    const int i = c >> p.vpd_log2;
+    const int h = p.head_offset + g * p.group_stride + i;
+    const bool valid = i < p.group_valid && h < p.heads;
     const long long strided = s * ss + h * hs + (c & dmask);
     if (kPack) {
       uint4 val = make_uint4(0, 0, 0, 0);
-      if (h < p.heads) val = __ldg(src + strided);
+      if (valid) val = __ldg(src + strided);
       dst[packed_base + idx] = val;
     } else {
-      if (h < p.heads) dst[strided] = __ldg(src + packed_base + idx);
+      if (valid) dst[strided] = __ldg(src + packed_base + idx);
     }
   }
 }

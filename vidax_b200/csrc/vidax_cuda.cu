@@ -244,11 +244,17 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
   if (units > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "too many work units");
   p.num_units = static_cast<int>(units);
 
-  auto kern = attn_fwd_kernel<DenseGeo>;
+  if (a->schedule != VX_SCHED_STATIC && a->schedule != VX_SCHED_DYNAMIC)
+    return fail(VX_EINVAL, "schedule must be VX_SCHED_STATIC or VX_SCHED_DYNAMIC");
+  const bool dynamic = a->schedule == VX_SCHED_DYNAMIC;
+  // STATIC: one CTA per SM striding over the units. DYNAMIC: one CTA per
+  // unit; running CTAs take over not-yet-launched ones through cluster launch
+  // control (persistent and balanced even when other kernels hold SMs).
+  auto kern = dynamic ? attn_fwd_kernel<DenseGeo, kSchedSteal> : attn_fwd_kernel<DenseGeo, kSchedStride>;
   if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
   int sms = 0;
   if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
-  dim3 grid(static_cast<unsigned>(std::min<long long>(units, sms)));
+  dim3 grid(static_cast<unsigned>(dynamic ? units : std::min<long long>(units, sms)));
   kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
@@ -274,7 +280,18 @@ static int head_slab(const vx_head_slab_args* a, vx_stream_t stream, bool pack) 
   p.seq = a->seq;
   p.heads = a->heads;
   p.groups = a->groups;
-  p.hg = (a->heads + a->groups - 1) / a->groups;
+  const int whole = (a->heads + a->groups - 1) / a->groups;
+  const bool sub = a->slab_heads != 0 || a->group_stride != 0 || a->head_offset != 0 ||
+                   a->group_valid != 0;
+  p.hg = sub ? a->slab_heads : whole;
+  p.group_stride = sub ? a->group_stride : whole;
+  p.head_offset = sub ? a->head_offset : 0;
+  p.group_valid = sub ? a->group_valid : whole;
+  if (p.hg <= 0 || p.group_stride < 0 || p.head_offset < 0 || p.group_valid < 0 ||
+      p.group_valid > p.hg)
+    return fail(VX_EINVAL, "bad sub-group selection (slab_heads %d, group_stride %d, "
+                "head_offset %d, group_valid %d)", a->slab_heads, a->group_stride,
+                a->head_offset, a->group_valid);
   for (int t = 0; t < 3; ++t) {
     p.src[t] = nullptr;
     p.dst[t] = nullptr;
@@ -512,7 +529,7 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.round_logits = a->round_logits ? 1 : 0;
 
-  auto kern = attn_fwd_kernel<NaGeoDefault>;
+  auto kern = attn_fwd_kernel<NaGeoDefault, kSchedSingle>;
   if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
   // One work unit per CTA: neighborhood units are short (tens of KV tiles),
   // and a fresh CTA per unit measured faster than the persistent hand-off.

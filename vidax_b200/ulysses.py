@@ -16,15 +16,19 @@ shape).
 Data path per batch item (rank r of P, local tokens S_loc, heads H):
 
 1. `vx_ulysses_pack` (one CUDA launch for q, k, v): strided (S_loc, H, D)
-   -> contiguous (P, S_loc, Hg, D), Hg = ceil(H / P), zero heads past H.
+   -> contiguous (P, S_loc, hs, D): a slice of hs heads of every rank's
+   head group (Hg = ceil(H / P) heads per rank, zero heads past H).
 2. three equal-split NCCL all-to-alls (tokens -> heads): rank r receives
-   (P_src, S_loc, Hg, D) == the full sequence (S, Hg, D) in natural token
-   order for its head group [r*Hg, (r+1)*Hg) -- the tiled
-   all_to_all(split_axis=2, concat_axis=1) of attention.py:379-381.
-3. the sm_100a attention kernel over (1, S, Hg, D), written in place as
-   (P, S_loc, Hg, D) -- already the heads -> tokens send layout.
+   (P_src, S_loc, hs, D) == the full sequence (S, hs, D) in natural token
+   order for its heads -- the tiled all_to_all(split_axis=2, concat_axis=1)
+   of attention.py:379-381, one slice at a time.
+3. the sm_100a attention kernel over (1, S, hs, D), written as
+   (P, S_loc, hs, D) -- already the heads -> tokens send layout.
 4. one NCCL all-to-all back (attention.py:388) and `vx_ulysses_unpack`
    into the strided (S_loc, H, D) output, dropping padded heads.
+
+The Hg heads are processed in about four slices so that the all-to-alls of
+one slice (on NCCL's stream) overlap the kernel of another.
 
 Unlike the reference (whose tiled all_to_all requires H % P == 0), head
 counts that do not divide P are padded with zero heads.
@@ -86,12 +90,17 @@ class HeadSlabArgs(ctypes.Structure):
         ("heads", ctypes.c_int32),
         ("head_dim", ctypes.c_int32),
         ("groups", ctypes.c_int32),
+        ("slab_heads", ctypes.c_int32),
+        ("group_stride", ctypes.c_int32),
+        ("head_offset", ctypes.c_int32),
+        ("group_valid", ctypes.c_int32),
     ]
 
 
-def _slab_call(fn_name: str, strided, packed, heads: int, groups: int) -> None:
+def _slab_call(fn_name: str, strided, packed, heads: int, groups: int, sub=None) -> None:
     """strided: list of (S_loc, H, D) views; packed: list of contiguous
-    (groups, S_loc, Hg, D) buffers."""
+    (groups, S_loc, Hg, D) buffers; `sub` = (slab_heads, group_stride,
+    head_offset, group_valid) selects a sub-group of every group."""
     a = HeadSlabArgs()
     a.num_tensors = len(strided)
     seq, _, d = strided[0].shape
@@ -106,6 +115,8 @@ def _slab_call(fn_name: str, strided, packed, heads: int, groups: int) -> None:
             a.src[i], a.dst[i] = p_t.data_ptr(), s_t.data_ptr()
         a.stride[i][0], a.stride[i][1] = s_t.stride(0), s_t.stride(1)
     a.seq, a.heads, a.head_dim, a.groups = seq, heads, d, groups
+    if sub is not None:
+        a.slab_heads, a.group_stride, a.head_offset, a.group_valid = sub
     lib = _lib.load()
     fn = getattr(lib, fn_name)
     fn.argtypes = [ctypes.POINTER(HeadSlabArgs), ctypes.c_void_p]
@@ -114,20 +125,22 @@ def _slab_call(fn_name: str, strided, packed, heads: int, groups: int) -> None:
     _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)))
 
 
-def pack_heads(strided, groups: int, out=None):
-    """(S_loc, H, D) strided views (1-3 tensors) -> contiguous (groups, S_loc, Hg, D)."""
+def pack_heads(strided, groups: int, out=None, sub=None):
+    """(S_loc, H, D) strided views (1-3 tensors) -> contiguous (groups, S_loc, Hg, D).
+    `sub` = (slab_heads, group_stride, head_offset, group_valid) packs only a
+    slice of every group (see vx_head_slab_args)."""
     seq, heads, d = strided[0].shape
-    hg = -(-heads // groups)
+    hg = -(-heads // groups) if sub is None else sub[0]
     if out is None:
         out = [torch.empty((groups, seq, hg, d), dtype=t.dtype, device=t.device) for t in strided]
-    _slab_call("vx_ulysses_pack", list(strided), list(out), heads, groups)
+    _slab_call("vx_ulysses_pack", list(strided), list(out), heads, groups, sub)
     return out
 
 
-def unpack_heads(packed, strided_out, heads: int) -> None:
+def unpack_heads(packed, strided_out, heads: int, sub=None) -> None:
     """contiguous (groups, S_loc, Hg, D) -> strided (S_loc, H, D) views, in place."""
     groups = packed[0].shape[0]
-    _slab_call("vx_ulysses_unpack", list(strided_out), list(packed), heads, groups)
+    _slab_call("vx_ulysses_unpack", list(strided_out), list(packed), heads, groups, sub)
 
 
 # ---------------------------------------------------------------- exchange
@@ -139,27 +152,75 @@ def exchange(send: torch.Tensor, group, out: Optional[torch.Tensor] = None) -> t
     return recv
 
 
-def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int]):
-    """One batch item: qb/kb/vb/ob are (S_loc, H, D) views."""
-    S_loc, H, D = qb.shape
-    sq, sk, sv = pack_heads([qb, kb, vb], P)
-    rq, rk, rv = exchange(sq, group), exchange(sk, group), exchange(sv, group)
-    Hg = rq.shape[2]
-    S = P * S_loc
-    kv_len = None
-    if kv_valid is not None and kv_valid < S:
-        kv_len = torch.full((1,), kv_valid, dtype=torch.int32, device=qb.device)
+def _sub_heads(hg: int, target_pieces: int = 4) -> int:
+    """Heads per pipelined piece: a divisor of hg giving about target_pieces."""
+    hs = max(1, hg // target_pieces)
+    while hg % hs:
+        hs -= 1
+    return hs
+
+
+def _timed_attention(q, k, v, sm_scale, kv_len, out):
     events = KERNEL_EVENTS
     if events is not None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-    o_full = flash_attention(rq.view(1, S, Hg, D), rk.view(1, S, Hg, D), rv.view(1, S, Hg, D),
-                             sm_scale, kv_len=kv_len)
+    # dynamic schedule: NCCL's all-to-all kernels run concurrently on some SMs
+    o = flash_attention(q, k, v, sm_scale, kv_len=kv_len, out=out, dynamic_schedule=True)
     if events is not None:
         e1.record()
         events.append((e0, e1))
-    ro = exchange(o_full.view(P, S_loc, Hg, D), group)
-    unpack_heads([ro], [ob], H)
+    return o
+
+
+def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int],
+                 pieces: int = 4):
+    """One batch item: qb/kb/vb/ob are (S_loc, H, D) views.
+
+    The rank's head group (Hg heads after the exchange) is split into pieces
+    of hs heads; piece j's three tokens->heads all-to-alls run on the NCCL
+    stream while the kernel computes piece j-1, and piece j's heads->tokens
+    all-to-all overlaps the kernel on piece j+1."""
+    S_loc, H, D = qb.shape
+    Hg = -(-H // P)
+    S = P * S_loc
+    hs = _sub_heads(Hg, pieces)
+    n = Hg // hs
+    kv_len = None
+    if kv_valid is not None and kv_valid < S:
+        kv_len = torch.full((1,), kv_valid, dtype=torch.int32, device=qb.device)
+    subs = [(hs, Hg, j * hs, hs) for j in range(n)]
+    sends = [pack_heads([qb, kb, vb], P, sub=sub) for sub in subs]   # each (P, S_loc, hs, D)
+    recvs, works = [None] * n, [None] * n
+
+    def start_in(j):
+        recvs[j] = [torch.empty_like(t) for t in sends[j]]
+        works[j] = [dist.all_to_all_single(r, t, group=group, async_op=True)
+                    for r, t in zip(recvs[j], sends[j])]
+
+    start_in(0)
+    back = []
+    for j in range(n):
+        if j + 1 < n:
+            start_in(j + 1)
+        for w in works[j]:
+            w.wait()
+        rq, rk, rv = (t.view(1, S, hs, D) for t in recvs[j])
+        o = _timed_attention(rq, rk, rv, sm_scale, kv_len, None)
+        ro = torch.empty((P, S_loc, hs, D), dtype=o.dtype, device=o.device)
+        back.append((ro, dist.all_to_all_single(ro, o.view(P, S_loc, hs, D), group=group,
+                                                 async_op=True)))
+        sends[j] = None  # release the send buffers of piece j
+    for (ro, w), sub in zip(back, subs):
+        w.wait()
+        unpack_heads([ro], [ob], H, sub=sub)
+
+
+def launches_per_layer(heads: int, world: int, batch: int = 1, pieces: int = 4) -> int:
+    """CUDA launches of this library per sequence-parallel layer (pack,
+    attention and unpack per pipelined piece and batch item)."""
+    hg = -(-heads // world)
+    return 3 * (hg // _sub_heads(hg, pieces)) * batch
 
 
 def sequence_parallel_self_attention(
