@@ -27,7 +27,7 @@ Data path per batch item (rank r of P, local tokens S_loc, heads H):
 4. one NCCL all-to-all back (attention.py:388) and `vx_ulysses_unpack`
    into the strided (S_loc, H, D) output, dropping padded heads.
 
-The Hg heads are processed in about four slices so that the all-to-alls of
+The Hg heads are processed in up to three slices so that the all-to-alls of
 one slice (on NCCL's stream) overlap the kernel of another.
 
 Unlike the reference (whose tiled all_to_all requires H % P == 0), head
@@ -152,12 +152,27 @@ def exchange(send: torch.Tensor, group, out: Optional[torch.Tensor] = None) -> t
     return recv
 
 
-def _sub_heads(hg: int, target_pieces: int = 4) -> int:
-    """Heads per pipelined piece: a divisor of hg giving about target_pieces."""
-    hs = max(1, hg // target_pieces)
-    while hg % hs:
-        hs -= 1
-    return hs
+def _pieces(hg: int):
+    """Head counts of the pipelined slices of a rank's hg heads: a small
+    first slice (its exchange is the one not hidden behind the kernel), then
+    up to two larger ones (fewer, bigger kernel launches keep the GPU full)."""
+    if hg <= 1:
+        return [hg]
+    first = max(1, hg // 5)
+    rest = hg - first
+    if rest <= 1:
+        return [first, rest]
+    return [first, rest - rest // 2, rest // 2]
+
+
+_side: dict = {}
+
+
+def _side_stream(device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _side:
+        _side[idx] = torch.cuda.Stream(device=idx)
+    return _side[idx]
 
 
 def _timed_attention(q, k, v, sm_scale, kv_len, out):
@@ -173,23 +188,23 @@ def _timed_attention(q, k, v, sm_scale, kv_len, out):
     return o
 
 
-def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int],
-                 pieces: int = 4):
+def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int]):
     """One batch item: qb/kb/vb/ob are (S_loc, H, D) views.
 
-    The rank's head group (Hg heads after the exchange) is split into pieces
-    of hs heads; piece j's three tokens->heads all-to-alls run on the NCCL
-    stream while the kernel computes piece j-1, and piece j's heads->tokens
-    all-to-all overlaps the kernel on piece j+1."""
+    The rank's head group (Hg heads after the exchange) is split into slices
+    (`_pieces`); slice j+1's three tokens->heads all-to-alls run on NCCL's
+    stream while the kernel computes slice j, and slice j's heads->tokens
+    all-to-all and unpack (on a side stream) overlap the kernel on slice j+1."""
     S_loc, H, D = qb.shape
     Hg = -(-H // P)
     S = P * S_loc
-    hs = _sub_heads(Hg, pieces)
-    n = Hg // hs
     kv_len = None
     if kv_valid is not None and kv_valid < S:
         kv_len = torch.full((1,), kv_valid, dtype=torch.int32, device=qb.device)
-    subs = [(hs, Hg, j * hs, hs) for j in range(n)]
+    sizes = _pieces(Hg)
+    offs = [sum(sizes[:j]) for j in range(len(sizes))]
+    subs = [(hs, Hg, off, hs) for hs, off in zip(sizes, offs)]
+    n = len(subs)
     sends = [pack_heads([qb, kb, vb], P, sub=sub) for sub in subs]   # each (P, S_loc, hs, D)
     recvs, works = [None] * n, [None] * n
 
@@ -198,9 +213,12 @@ def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optio
         works[j] = [dist.all_to_all_single(r, t, group=group, async_op=True)
                     for r, t in zip(recvs[j], sends[j])]
 
+    comp = torch.cuda.current_stream(qb.device)
+    side = _side_stream(qb.device)
+    side.wait_stream(comp)
     start_in(0)
-    back = []
-    for j in range(n):
+    for j, sub in enumerate(subs):
+        hs = sub[0]
         if j + 1 < n:
             start_in(j + 1)
         for w in works[j]:
@@ -208,19 +226,20 @@ def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optio
         rq, rk, rv = (t.view(1, S, hs, D) for t in recvs[j])
         o = _timed_attention(rq, rk, rv, sm_scale, kv_len, None)
         ro = torch.empty((P, S_loc, hs, D), dtype=o.dtype, device=o.device)
-        back.append((ro, dist.all_to_all_single(ro, o.view(P, S_loc, hs, D), group=group,
-                                                 async_op=True)))
-        sends[j] = None  # release the send buffers of piece j
-    for (ro, w), sub in zip(back, subs):
-        w.wait()
-        unpack_heads([ro], [ob], H, sub=sub)
+        w_out = dist.all_to_all_single(ro, o.view(P, S_loc, hs, D), group=group, async_op=True)
+        sends[j] = None  # release the send buffers of slice j
+        with torch.cuda.stream(side):
+            w_out.wait()                       # the side stream waits for the exchange
+            unpack_heads([ro], [ob], H, sub=sub)
+            ro.record_stream(side)
+    comp.wait_stream(side)
 
 
-def launches_per_layer(heads: int, world: int, batch: int = 1, pieces: int = 4) -> int:
+def launches_per_layer(heads: int, world: int, batch: int = 1) -> int:
     """CUDA launches of this library per sequence-parallel layer (pack,
-    attention and unpack per pipelined piece and batch item)."""
+    attention and unpack per pipelined slice and batch item)."""
     hg = -(-heads // world)
-    return 3 * (hg // _sub_heads(hg, pieces)) * batch
+    return 3 * len(_pieces(hg)) * batch
 
 
 def sequence_parallel_self_attention(
