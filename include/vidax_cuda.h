@@ -160,6 +160,15 @@ int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out);
 int vx_memcpy_rows_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
                          int64_t row_bytes, int64_t rows, vx_stream_t stream);
 
+/* Self-test of the bounded-wait machinery (failure detection without a GPU
+ * fault): runs one CTA that waits on an mbarrier nothing arrives on, through
+ * the same bounded wait the kernels use, with a limit of `limit_cycles` SM
+ * cycles. The wait gives up, raises the CTA's abort flag and records status
+ * bit 16 in the device status word; returns VX_ETIMEOUT with *status_out set
+ * to the status word (VX_ECUDA if the wait did not behave as specified). The
+ * context stays usable; clear the word with vx_device_status(.., 1). */
+int vx_selftest_wait_timeout(int64_t limit_cycles, int* status_out);
+
 #ifdef __cplusplus
 }
 #endif

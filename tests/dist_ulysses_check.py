@@ -38,6 +38,26 @@ def main():
             mx, mean = compare(got, sdpa(q, k, v))
             print(f"B={B} S={S} H={H}: max {mx:.3g} mean {mean:.3g}", flush=True)
             ok = ok and mx <= 2e-2 and mean <= 2e-3
+    # joint [text; visual] layout (CogVideoX): text replicated, visual chunked
+    for (B, T_len, S, H) in [(1, 226, 1024, 8), (2, 77, 512, 6)]:
+        seed = 950 + T_len + S
+        q, k, v = seeded_qkv((B, T_len + S, H, 128), seed)
+        sl = S // world
+        def local(x):
+            return np.concatenate([x[:, :T_len], x[:, T_len + rank * sl:T_len + (rank + 1) * sl]], axis=1)
+        mine = [torch.from_numpy(np.ascontiguousarray(local(x))).cuda().bfloat16() for x in (q, k, v)]
+        out = vx.sequence_parallel_joint_self_attention(*mine, T_len, "sp")
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out.contiguous())
+        if rank == 0:
+            ref = sdpa(q, k, v)
+            txt = gathered[0][:, :T_len].float().cpu().numpy()
+            vis = torch.cat([g[:, T_len:] for g in gathered], dim=1).float().cpu().numpy()
+            got = np.concatenate([txt, vis], axis=1)
+            mx, mean = compare(got, ref)
+            same_txt = all(torch.equal(gathered[0][:, :T_len], g[:, :T_len]) for g in gathered)
+            print(f"joint B={B} T={T_len} S={S} H={H}: max {mx:.3g} mean {mean:.3g} txt-replicated {same_txt}", flush=True)
+            ok = ok and mx <= 2e-2 and mean <= 2e-3 and same_txt
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.broadcast(flag, 0)
     vx.unregister_axis("sp")

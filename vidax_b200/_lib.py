@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "vx_ulysses_pack",
     "vx_ulysses_unpack",
     "vx_memcpy_rows_async",
+    "vx_selftest_wait_timeout",
 )
 
 
@@ -124,6 +125,21 @@ def check(rc: int) -> None:
     if rc == VX_EINVAL:
         raise VxInvalid(rc, msg)
     raise VxError(rc, msg)
+
+
+def selftest_wait_timeout(limit_cycles: int = 2_000_000) -> int:
+    """Runs the bounded-wait self-test kernel (see vx_selftest_wait_timeout)
+    and returns the device status word it left (bit 16 set when the wait gave
+    up as designed)."""
+    lib = load()
+    fn = lib.vx_selftest_wait_timeout
+    fn.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_int)]
+    fn.restype = ctypes.c_int
+    out = ctypes.c_int(0)
+    rc = fn(limit_cycles, ctypes.byref(out))
+    if rc != VX_ETIMEOUT:
+        check(rc if rc != VX_OK else VX_ECUDA)
+    return out.value
 
 
 def device_status(clear: bool = True) -> int:

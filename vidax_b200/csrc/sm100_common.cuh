@@ -22,6 +22,7 @@ enum DeviceStatus : int {
   kDevTimeoutMma = 2,       // MMA issuer waited too long for data / P
   kDevTimeoutSoftmax = 4,   // softmax waited too long for S / O
   kDevTimeoutDrain = 8,     // drain of in-flight async work timed out
+  kDevSelfTest = 16,        // the wait-timeout self-test expired (expected)
 };
 
 // ~4 s at 2 GHz. A legitimate wait inside these kernels lasts microseconds.
@@ -64,14 +65,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // (after raising the CTA abort flag and recording `code` in *status) when the
 // wait exceeds the cycle limit, or when another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+                                          int* status, int code,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0u) {
       if (*abort_flag) return false;
-      if (clock64() - t0 > kWaitLimitCycles) {
+      if (clock64() - t0 > limit) {
         *abort_flag = 1;
         atomicOr(status, code);
         return false;

@@ -47,6 +47,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 // Device status word: kernels OR timeout codes into it (one instance per
 // device context).
 __device__ int g_vx_status;
+// Report of the bounded-wait self-test kernel: {wait succeeded, abort flag}.
+__device__ int g_vx_selftest[2];
 
 namespace {
 
@@ -333,6 +335,26 @@ int vx_ulysses_unpack(const vx_head_slab_args* a, vx_stream_t stream) {
 
 namespace {
 
+// One CTA waits, through the same bounded mbarrier wait the attention kernels
+// use, on a barrier nothing ever arrives on; the wait must give up after
+// `limit` SM cycles, raise the abort flag and record kDevSelfTest.
+__global__ void selftest_wait_kernel(int* status, long long limit, int* result) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    vx::mbar_init(vx::smem_u32(&bar), 1);
+    vx::fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = vx::mbar_wait(vx::smem_u32(&bar), 0, &abort_flag, status, vx::kDevSelfTest,
+                                  limit);
+    result[0] = ok ? 1 : 0;
+    result[1] = abort_flag;
+  }
+}
+
 constexpr int kNaKT = 2, kNaKH = 4, kNaKW = 16;
 using NaGeoDefault = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW>;
 
@@ -556,4 +578,30 @@ extern "C" int vx_memcpy_rows_async(void* dst, int64_t dst_pitch, const void* sr
                                     reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
   return VX_OK;
+}
+
+extern "C" int vx_selftest_wait_timeout(int64_t limit_cycles, int* status_out) {
+  if (limit_cycles <= 0 || limit_cycles > 4000000000LL)
+    return fail(VX_EINVAL, "limit_cycles must be in (0, 4e9]");
+  int dev;
+  int rc = current_device(&dev);
+  if (rc != VX_OK) return rc;
+  int* status = nullptr;
+  if ((rc = status_word(dev, &status)) != VX_OK) return rc;
+  void* d_result = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&d_result, g_vx_selftest);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(selftest)");
+  selftest_wait_kernel<<<1, 32>>>(status, static_cast<long long>(limit_cycles),
+                                  static_cast<int*>(d_result));
+  e = cudaGetLastError();
+  int h[2] = {-1, -1};
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(h, g_vx_selftest, sizeof(h));
+  if (e != cudaSuccess) return cuda_fail(e, "selftest kernel");
+  if (h[0] != 0 || h[1] != 1)
+    return fail(VX_ECUDA, "self-test wait did not time out as expected (ok=%d abort=%d)", h[0], h[1]);
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_vx_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status)");
+  if (status_out) *status_out = v;
+  return VX_ETIMEOUT;
 }
