@@ -21,10 +21,10 @@ vidax code around them -- window starts, gather indices, key ordering, the
 scan/vmap structure, dtype handling, dispatch, default scale and the Ulysses
 split/concat axes -- is the reference's own.
 
-Run from the repository root, where /root/reference exists:
-    python tests/golden/make_golden.py
-The fixtures are committed; tests only read them (the reference does not
-exist on the GPU box).
+Run from the repository root with the path of a vidax checkout:
+    python tests/golden/make_golden.py <path-to-vidax>
+The fixtures are committed; tests only read them (the reference checkout is
+not needed to run the tests).
 """
 from __future__ import annotations
 
@@ -37,7 +37,7 @@ import types
 import ml_dtypes
 import numpy as np
 
-REF = os.environ.get("VIDAX_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("VIDAX_REFERENCE", "")
 OUT_DIR = os.path.dirname(os.path.abspath(__file__))
 BF16 = ml_dtypes.bfloat16
 
@@ -237,8 +237,8 @@ def gen_attention():
 
 
 def main():
-    if not os.path.isdir(REF):
-        sys.exit(f"reference not found at {REF}")
+    if not REF or not os.path.isdir(REF):
+        sys.exit("usage: make_golden.py <path-to-vidax-checkout>")
     na = gen_na3d()
     np.savez_compressed(os.path.join(OUT_DIR, "na3d_reference.npz"), **na)
     at = gen_attention()
