@@ -157,9 +157,9 @@ def test_empty_keys_give_zero_rows():
 @pytest.mark.gpu
 def test_unsupported_requests_raise():
     import vidax_b200 as vx
-    q = torch.zeros((1, 16, 2, 64), dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros((1, 16, 2, 96), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(NotImplementedError):
-        vx.flash_attention(q, q, q, 0.125)  # head_dim 64 not built for dense yet
+        vx.flash_attention(q, q, q, 0.125)  # head_dim 96 is not built
     q = torch.zeros((1, 16, 2, 128), dtype=torch.float32, device="cuda")
     with pytest.raises(NotImplementedError):
         vx.flash_attention(q, q, q, 0.125)
@@ -199,4 +199,19 @@ def test_dynamic_schedule_matches_static():
     assert _status_clean()
     assert torch.equal(o_static, o_dyn)
     mx, mean = compare(_host(o_dyn), sdpa(q, k, v))
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,Sq,Sk,H,Hkv", [(1, 300, 300, 4, 4), (2, 1000, 777, 3, 1), (1, 1, 5, 2, 2),
+                                           (1, 4096, 4096, 2, 2)])
+@pytest.mark.parametrize("dynamic", [False, True])
+def test_head_dim_64(B, Sq, Sk, H, Hkv, dynamic):
+    import vidax_b200 as vx
+    q, = seeded_qkv((B, Sq, H, 64), 81 + Sq, n=1)
+    k, v = seeded_qkv((B, Sk, Hkv, 64), 82 + Sk, n=2)
+    out = vx.flash_attention(_dev(q), _dev(k), _dev(v), 64 ** -0.5, dynamic_schedule=dynamic)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    mx, mean = compare(_host(out), sdpa(q, k, v))
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

@@ -133,3 +133,23 @@ def test_cfg4_sampled_positions():
     got = out.float().cpu().numpy()[0][pos[:, 0], pos[:, 1], pos[:, 2]][None]
     mx, mean = compare(got, ref)
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,kernel", [
+    ((1, 4, 9, 17, 2), (3, 5, 5)),
+    ((1, 5, 12, 20, 2), (3, 7, 7)),
+    ((1, 12, 13, 14, 1), (11, 11, 11)),   # the LTX-2.5 stage-5 window
+    ((2, 3, 6, 9, 2), (3, 3, 3)),
+])
+def test_na3d_head_dim_64(shape, kernel):
+    """The production LTX-2.5 decoder runs neighborhood attention at head_dim 64."""
+    import vidax_b200 as vx
+    B, T, H, W, NH = shape
+    q, k, v = seeded_qkv((B, T, H, W, NH, 64), 700 + T * 7 + W, n=3)
+    q = to_bf16(q * np.float32(64 ** -0.5))
+    out = vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), kernel)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    mx, mean = compare(out.float().cpu().numpy(), na3d(q, k, v, kernel))
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

@@ -38,14 +38,28 @@
 namespace vx {
 namespace attn {
 
-constexpr int kHeadDim = 128;
 constexpr int kBlockM = 128;  // query rows per tile (one softmax warpgroup)
 constexpr int kBlockN = 128;  // keys per K/V tile
 constexpr int kStages = 2;
 constexpr int kThreads = 320;
-constexpr uint32_t kTileBytes = 128u * 128u * 2u;  // one 128x128 bf16 tile
-constexpr uint32_t kHalfBytes = kTileBytes / 2;     // 128 rows x 64 cols (128B rows)
+constexpr uint32_t kHalfBytes = 128u * 64u * 2u;  // 128 rows x 64 cols: one 128B-swizzle slab
 constexpr float kRescaleThreshold = 8.0f;
+
+// Head-dimension dependent sizes (head_dim 64 or 128). A 128-row tile of
+// head_dim D is D/64 swizzle slabs of kHalfBytes.
+template <int HD>
+struct Dims {
+  static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+  static constexpr int kHeadDim = HD;
+  static constexpr int kHalves = HD / 64;
+  static constexpr uint32_t kTileBytes = 128u * HD * 2u;
+  static constexpr uint32_t kSmemQ = 0;
+  static constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
+  static constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
+  static constexpr uint32_t kSmemBar = kSmemV + kStages * kTileBytes;
+  static constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + control block + alignment
+  static constexpr uint32_t kTmemO = 256;                        // O_t at kTmemO + HD * t
+};
 
 // Softmax tuning knobs (compile-time): every kPolyEvery-th pair of
 // exponentials goes through the FMA-pipe polynomial (0 = all on MUFU);
@@ -63,11 +77,6 @@ constexpr int kPolyEvery = VX_POLY_EVERY;
 constexpr bool kSplitP = VX_SPLIT_P != 0;
 constexpr bool kPackedF32x2 = VX_PACKED_F32X2 != 0;
 
-constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
-constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
-constexpr uint32_t kSmemBar = kSmemV + kStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + barriers + alignment slack
 
 // barrier slots
 enum : int {
@@ -87,15 +96,19 @@ enum : int {
   kClc = 24,       // 1: cluster-launch-control response landed
   kNumBars = 25,
 };
-constexpr uint32_t kTmemSlotOff = kSmemBar + 8 * kNumBars;
+// control block (offsets from the barrier base, which is 1024-aligned)
+constexpr uint32_t kTmemSlotOff = 8 * kNumBars;
 constexpr uint32_t kAbortOff = kTmemSlotOff + 4;
 constexpr uint32_t kUnitRingOff = kAbortOff + 4;                   // 2 ints
 constexpr uint32_t kClcRespOff = (kUnitRingOff + 8 + 15) & ~15u;   // 16 bytes, 16-aligned
-static_assert(kClcRespOff + 16 <= kSmemBar + 256, "control block exceeds its reservation");
+static_assert(kClcRespOff + 16 <= 256, "control block exceeds its reservation");
 constexpr int kUnitConsumers = 1 + 256;  // MMA issuer + every softmax thread
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, false, false);  // Q K^T: both K-major
-constexpr uint32_t kIdescO = idesc_bf16_f32(128, 128, false, true);   // P V : V is N-major
+template <int HD>
+__host__ __device__ constexpr uint32_t idesc_pv() {  // P V: V is N-major
+  return idesc_bf16_f32(128, HD, false, true);
+}
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 
@@ -105,9 +118,10 @@ __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); 
 // base descriptors; the per-step offsets are compile-time constants added to
 // the start-address field (in 16-byte units, no carry out of the field since
 // shared memory is below 256 KB).
+template <int HD>
 __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint64_t q_desc, uint64_t k_desc) {
 #pragma unroll
-  for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+  for (int kk = 0; kk < HD / 16; ++kk) {
     const uint64_t off = static_cast<uint64_t>(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
     mma_ss(tmem_s, q_desc + off, k_desc + off, kIdescS, kk > 0 ? 1u : 0u);
   }
@@ -119,13 +133,14 @@ __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint64_t q_desc, uint6
 // byte offset). `half` selects keys [0, 64) or [64, 128) of the tile (4 MMAs
 // each), so the first half can run while the softmax still produces the
 // second.
+template <int HD>
 __device__ __forceinline__ void issue_pv_half(uint32_t tmem_o, uint32_t tmem_p, uint64_t v_desc,
                                               int half, bool accumulate) {
 #pragma unroll
   for (int k4 = 0; k4 < 4; ++k4) {
     const int kk = half * 4 + k4;
-    mma_ts(tmem_o, tmem_p + kk * 8, v_desc + static_cast<uint64_t>((kk * 2048) >> 4), kIdescO,
-           (accumulate || kk > 0) ? 1u : 0u);
+    mma_ts(tmem_o, tmem_p + kk * 8, v_desc + static_cast<uint64_t>((kk * 2048) >> 4),
+           idesc_pv<HD>(), (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
@@ -144,15 +159,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ typename Geo::Params p) {
+  using Dm = Dims<Geo::kHeadDim>;
+  constexpr int HD = Geo::kHeadDim;
+  constexpr uint32_t kTileBytes = Dm::kTileBytes;
+  constexpr uint32_t kSmemQ = Dm::kSmemQ, kSmemK = Dm::kSmemK, kSmemV = Dm::kSmemV;
+  constexpr uint32_t kSmemBar = Dm::kSmemBar;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   auto bar = [&](int i) -> uint32_t { return sbase + kSmemBar + 8u * i; };
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kTmemSlotOff);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
+  volatile uint32_t* tmem_slot =
+      reinterpret_cast<volatile uint32_t*>(smem + kSmemBar + kTmemSlotOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemBar + kAbortOff);
   int* status = p.status;
-  volatile int* unit_ring = reinterpret_cast<volatile int*>(smem + kUnitRingOff);
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(smem + kSmemBar + kUnitRingOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -183,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 9) {
-    tmem_alloc(sbase + kTmemSlotOff, 512);
+    tmem_alloc(sbase + kSmemBar + kTmemSlotOff, 512);
     tmem_relinquish();
   }
   if (warp == 8 && lane == 0) {
@@ -222,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint64_t pol_q = l2_policy_evict_first();
       const uint64_t pol_kv = l2_policy_evict_last();
-      const uint32_t clc_resp = sbase + kClcRespOff;
+      const uint32_t clc_resp = sbase + kSmemBar + kClcRespOff;
       uint32_t g = 0;   // global index of the unit's first KV tile
       int qi = 0;       // units with work issued
       int last_pair = -1;
@@ -349,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (geo.needs(t, 0)) {
-            issue_qk(tmem + 128 * t, q_desc[t], k_desc0 + ((g % kStages) ? kStageStep : 0));
+            issue_qk<HD>(tmem + 128 * t, q_desc[t], k_desc0 + ((g % kStages) ? kStageStep : 0));
             tc_commit(bar(kSFull + t));
           }
         }
@@ -386,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   break;
                 }
                 tc_fence_after();
-                issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
+                issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
               }
               if (!mbar_wait(bar(kPHi + t), par, abort_flag, status, kDevTimeoutMma)) {
                 ok = false;
@@ -394,14 +415,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               tc_fence_after();
               if (!kSplitP)
-                issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
-              issue_pv_half(tmem + 256 + 128 * t, tmem + 128 * t, v_d, 1, true);
+                issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
+              issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 1, true);
               first_pv[t] = false;
               ++p_count[t];
               if (j == last[t]) tc_commit(bar(kOFull + t));
             }
             if (has_next && geo.needs(t, j + 1)) {
-              issue_qk(tmem + 128 * t, q_desc[t], k_next);
+              issue_qk<HD>(tmem + 128 * t, q_desc[t], k_next);
               tc_commit(bar(kSFull + t));
             }
           }
@@ -430,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t t_s = tmem + wg * 128 + lane_off;
-    const uint32_t t_o = tmem + 256 + wg * 128 + lane_off;
+    const uint32_t t_o = tmem + Dm::kTmemO + wg * HD + lane_off;
     const float scale_log2 = p.scale_log2;
     int s_count = 0;  // S tiles consumed by this query tile (all units)
     int o_units = 0;  // units in which this query tile accumulated O
@@ -483,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // issued after that PV and its commit tracks every earlier MMA.
           // Rescale this warp's 32 rows of O.
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < HD / 32; ++c) {
             uint32_t orr[32];
             tmem_ld32(t_o + c * 32, orr);
             tmem_wait_ld(orr);
@@ -556,9 +577,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      uint32_t pk[4][16];
+      uint32_t pk[HD / 32][16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t orr[32];
         tmem_ld32(t_o + c * 32, orr);
         tmem_wait_ld(orr);
@@ -572,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bar(kOFree + wg));
       ++o_units;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) geo.store_row_chunk(wg, row, c, pk[c]);
+      for (int c = 0; c < HD / 32; ++c) geo.store_row_chunk(wg, row, c, pk[c]);
       // natural-log LSE of the row's scaled logits
       const float lse = l_sum > 0.f ? (m_used + __log2f(l_sum)) * 0.69314718055994531f
                                     : neg_inf();
@@ -604,7 +625,9 @@ struct DenseParams {
   float scale_log2;
 };
 
+template <int HD>
 struct DenseGeo {
+  static constexpr int kHeadDim = HD;
   using Params = DenseParams;
   const DenseParams& p;
   int b, h, hk, q0, kv_valid;
@@ -628,13 +651,15 @@ struct DenseGeo {
   __device__ int last_tile(int) const { return num_kv_tiles() - 1; }
   __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
                          uint64_t pol) const {
-    tma_load_4d(dst, tm, bar, 0, h, q0 + t * kBlockM, b, pol);
-    tma_load_4d(dst + kHalfBytes, tm, bar, 64, h, q0 + t * kBlockM, b, pol);
+#pragma unroll
+    for (int c = 0; c < HD / 64; ++c)
+      tma_load_4d(dst + c * kHalfBytes, tm, bar, 64 * c, h, q0 + t * kBlockM, b, pol);
   }
   __device__ void load_kv(const CUtensorMap* tm, int j, uint32_t dst, uint32_t bar,
                           uint64_t pol) const {
-    tma_load_4d(dst, tm, bar, 0, hk, j * kBlockN, b, pol);
-    tma_load_4d(dst + kHalfBytes, tm, bar, 64, hk, j * kBlockN, b, pol);
+#pragma unroll
+    for (int c = 0; c < HD / 64; ++c)
+      tma_load_4d(dst + c * kHalfBytes, tm, bar, 64 * c, hk, j * kBlockN, b, pol);
   }
   __device__ void softmax_setup(int wg, int row) { row_global = q0 + wg * kBlockM + row; }
   __device__ void mask_scores(int j, uint32_t (&sr)[4][32]) const {
@@ -661,7 +686,7 @@ struct DenseGeo {
     if (row_global >= p.Sq) return;
     uint4* dst = reinterpret_cast<uint4*>(row_ptr());
 #pragma unroll
-    for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+    for (int i = 0; i < HD / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
     if (p.lse != nullptr)
       p.lse[(static_cast<long long>(b) * p.H + h) * p.Sq + row_global] = neg_inf();
   }
@@ -723,8 +748,9 @@ __device__ __forceinline__ uint32_t bit_range(int lo, int hi, int n) {
   return upto_hi & ~upto_lo;
 }
 
-template <int KT, int KH, int KW>
+template <int KT, int KH, int KW, int HD>
 struct NaGeo {
+  static constexpr int kHeadDim = HD;
   static_assert(KT * KH * KW == 128, "key tile must hold 128 keys");
   static_assert(KW == 8 || KW == 16 || KW == 32, "key tile width 8, 16 or 32");
   using Params = NaParams;
@@ -818,16 +844,18 @@ struct NaGeo {
   __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
                          uint64_t pol) const {
     const int bt = b * p.T + org[t][0];
-    tma_load_5d(dst, tm, bar, 0, head, org[t][2], org[t][1], bt, pol);
-    tma_load_5d(dst + kHalfBytes, tm, bar, 64, head, org[t][2], org[t][1], bt, pol);
+#pragma unroll
+    for (int c = 0; c < HD / 64; ++c)
+      tma_load_5d(dst + c * kHalfBytes, tm, bar, 64 * c, head, org[t][2], org[t][1], bt, pol);
   }
   __device__ void load_kv(const CUtensorMap* tm, int j, uint32_t dst, uint32_t bar,
                           uint64_t pol) const {
     int o[3];
     tile_origin(j, o);
     const int bt = b * p.T + o[0];
-    tma_load_5d(dst, tm, bar, 0, head_kv, o[2], o[1], bt, pol);
-    tma_load_5d(dst + kHalfBytes, tm, bar, 64, head_kv, o[2], o[1], bt, pol);
+#pragma unroll
+    for (int c = 0; c < HD / 64; ++c)
+      tma_load_5d(dst + c * kHalfBytes, tm, bar, 64 * c, head_kv, o[2], o[1], bt, pol);
   }
   __device__ void softmax_setup(int t, int row) {
     const int qw = p.qbox[2], qh = p.qbox[1];
@@ -886,7 +914,7 @@ struct NaGeo {
     if (!row_valid) return;
     uint4* dst = reinterpret_cast<uint4*>(row_ptr());
 #pragma unroll
-    for (int i = 0; i < 16; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+    for (int i = 0; i < HD / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
   }
   __device__ void store_lse(int, int, float) const {}
 };

@@ -192,8 +192,8 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
   if (a->heads_q % a->heads_kv != 0)
     return fail(VX_EINVAL, "heads_q (%d) must be a multiple of heads_kv (%d)", a->heads_q,
                 a->heads_kv);
-  if (a->head_dim != kHeadDim)
-    return fail(VX_EUNSUPPORTED, "head_dim %d (this build implements %d)", a->head_dim, kHeadDim);
+  if (a->head_dim != 64 && a->head_dim != 128)
+    return fail(VX_EUNSUPPORTED, "head_dim %d (this build implements 64 and 128)", a->head_dim);
   if (!(a->scale > 0.f) || !std::isfinite(a->scale))
     return fail(VX_EUNSUPPORTED, "softmax scale must be finite and > 0 (got %g)", (double)a->scale);
   if (a->batch > 65535 || a->heads_q > 65535)
@@ -214,13 +214,14 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
 
   // Key tensors need at least one row for a valid tensor map; with seq_k == 0
   // every output row is zero and no K/V tile is loaded.
+  const int HD = a->head_dim;
   CUtensorMap tq, tk, tv;
-  if ((rc = bshd_tmap(&tq, "q", a->q, a->q_stride, a->batch, a->seq_q, a->heads_q, kHeadDim)) != VX_OK)
+  if ((rc = bshd_tmap(&tq, "q", a->q, a->q_stride, a->batch, a->seq_q, a->heads_q, HD)) != VX_OK)
     return rc;
   if (a->seq_k > 0) {
-    if ((rc = bshd_tmap(&tk, "k", a->k, a->k_stride, a->batch, a->seq_k, a->heads_kv, kHeadDim)) != VX_OK)
+    if ((rc = bshd_tmap(&tk, "k", a->k, a->k_stride, a->batch, a->seq_k, a->heads_kv, HD)) != VX_OK)
       return rc;
-    if ((rc = bshd_tmap(&tv, "v", a->v, a->v_stride, a->batch, a->seq_k, a->heads_kv, kHeadDim)) != VX_OK)
+    if ((rc = bshd_tmap(&tv, "v", a->v, a->v_stride, a->batch, a->seq_k, a->heads_kv, HD)) != VX_OK)
       return rc;
   } else {
     tk = tq;  // never dereferenced: with no keys every output row is zero
@@ -252,12 +253,23 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
   // STATIC: one CTA per SM striding over the units. DYNAMIC: one CTA per
   // unit; running CTAs take over not-yet-launched ones through cluster launch
   // control (persistent and balanced even when other kernels hold SMs).
-  auto kern = dynamic ? attn_fwd_kernel<DenseGeo, kSchedSteal> : attn_fwd_kernel<DenseGeo, kSchedStride>;
-  if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
   int sms = 0;
   if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
   dim3 grid(static_cast<unsigned>(dynamic ? units : std::min<long long>(units, sms)));
-  kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (HD == 128) {
+    auto kern = dynamic ? attn_fwd_kernel<DenseGeo<128>, kSchedSteal>
+                        : attn_fwd_kernel<DenseGeo<128>, kSchedStride>;
+    constexpr uint32_t smem = Dims<128>::kSmemBytes;
+    if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
+    kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  } else {
+    auto kern = dynamic ? attn_fwd_kernel<DenseGeo<64>, kSchedSteal>
+                        : attn_fwd_kernel<DenseGeo<64>, kSchedStride>;
+    constexpr uint32_t smem = Dims<64>::kSmemBytes;
+    if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
+    kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_fwd launch");
   return VX_OK;
@@ -356,7 +368,8 @@ __global__ void selftest_wait_kernel(int* status, long long limit, int* result) 
 }
 
 constexpr int kNaKT = 2, kNaKH = 4, kNaKW = 16;
-using NaGeoDefault = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW>;
+template <int HD>
+using NaGeoDefault = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW, HD>;
 
 int na_start_host(int i, int L, int k) { return std::min(std::max(i - k / 2, 0), L - k); }
 
@@ -476,8 +489,8 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
   if (a->heads % a->heads_kv != 0) return fail(VX_EINVAL, "heads must be a multiple of heads_kv");
   if (a->kernel_t < 1 || a->kernel_h < 1 || a->kernel_w < 1)
     return fail(VX_EINVAL, "kernel sizes must be >= 1");
-  if (a->head_dim != kHeadDim)
-    return fail(VX_EUNSUPPORTED, "head_dim %d (this build implements %d)", a->head_dim, kHeadDim);
+  if (a->head_dim != 64 && a->head_dim != 128)
+    return fail(VX_EUNSUPPORTED, "head_dim %d (this build implements 64 and 128)", a->head_dim);
   if (!(a->scale > 0.f) || !std::isfinite(a->scale))
     return fail(VX_EUNSUPPORTED, "scale must be finite and > 0");
   if (a->batch == 0 || a->T == 0 || a->H == 0 || a->W == 0) return VX_OK;
@@ -512,11 +525,12 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
 
   const int kv_box[3] = {kNaKT, kNaKH, kNaKW};
   CUtensorMap tq, tk, tv;
-  if ((rc = na_tmap(&tq, "q", a->q, a->q_stride, a->batch, a->T, a->H, a->W, a->heads, kHeadDim, ch.qbox)) != VX_OK)
+  const int HD = a->head_dim;
+  if ((rc = na_tmap(&tq, "q", a->q, a->q_stride, a->batch, a->T, a->H, a->W, a->heads, HD, ch.qbox)) != VX_OK)
     return rc;
-  if ((rc = na_tmap(&tk, "k", a->k, a->k_stride, a->batch, a->T, a->H, a->W, a->heads_kv, kHeadDim, kv_box)) != VX_OK)
+  if ((rc = na_tmap(&tk, "k", a->k, a->k_stride, a->batch, a->T, a->H, a->W, a->heads_kv, HD, kv_box)) != VX_OK)
     return rc;
-  if ((rc = na_tmap(&tv, "v", a->v, a->v_stride, a->batch, a->T, a->H, a->W, a->heads_kv, kHeadDim, kv_box)) != VX_OK)
+  if ((rc = na_tmap(&tv, "v", a->v, a->v_stride, a->batch, a->T, a->H, a->W, a->heads_kv, HD, kv_box)) != VX_OK)
     return rc;
 
   NaParams p;
@@ -551,12 +565,21 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.round_logits = a->round_logits ? 1 : 0;
 
-  auto kern = attn_fwd_kernel<NaGeoDefault, kSchedSingle>;
-  if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, kSmemBytes)) != VX_OK) return rc;
   // One work unit per CTA: neighborhood units are short (tens of KV tiles),
   // and a fresh CTA per unit measured faster than the persistent hand-off.
   dim3 grid(static_cast<unsigned>(units));
-  kern<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (HD == 128) {
+    auto kern = attn_fwd_kernel<NaGeoDefault<128>, kSchedSingle>;
+    constexpr uint32_t smem = Dims<128>::kSmemBytes;
+    if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
+    kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  } else {
+    auto kern = attn_fwd_kernel<NaGeoDefault<64>, kSchedSingle>;
+    constexpr uint32_t smem = Dims<64>::kSmemBytes;
+    if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
+    kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "na3d_fwd launch");
   return VX_OK;
