@@ -177,6 +177,9 @@ def kernel_case(name: str, dev):
     cfg2          BASELINE config 2: (1, 32760, 40, 128), per-head factors U[0.5, 2]
     cfg4          BASELINE config 4: NA over (1, 21, 30, 52, 24, 128), window 5x9x9
     na3d:T,H,W,NH window 5x9x9
+    prologue:S,H,P  fused RMSNorm(dim) + RoPE + Ulysses send packing of q, k, v
+                  (S tokens, H heads, D=128, P destination ranks); its work is
+                  algorithmic HBM bytes, not FLOPs (see kernel_case_bytes)
     Returns (callable, algorithmic FLOPs per launch, description).
     """
     import torch
@@ -211,7 +214,30 @@ def kernel_case(name: str, dev):
         fl = vx.na3d_flops(1, t, hh, w, nh, D, (5, 9, 9))
         return (lambda: vx.neighborhood_attention_3d(q, k, v, (5, 9, 9))), fl, \
             f"neighborhood attention (1, {t}, {hh}, {w}, {nh}, {D}), window 5x9x9"
+    if name.startswith("prologue:"):
+        from vidax_b200.prologue import norm_rope_pack
+        from vidax_b200.ulysses import _pieces
+        s, h, p = (int(x) for x in name.split(":")[1].split(","))
+        xs = [rnd((1, s, h * D)) for _ in range(3)]
+        wq, wk = (1.0 + 0.1 * torch.randn(h * D, generator=gen, device=dev) for _ in range(2))
+        ang = torch.rand((s, D // 2), generator=gen, device=dev) * 100.0
+        rope = (torch.cos(ang), torch.sin(ang))
+        hg = -(-h // p)
+        slices = _pieces(hg) if p > 1 else None
+        out = [torch.empty((1, p * s * hg * D), dtype=torch.bfloat16, device=dev) for _ in range(3)]
+        return (lambda: norm_rope_pack(xs, h, norm_weights=[wq, wk, None], rope=rope, groups=p,
+                                       slices=slices, out=out)), 0.0, \
+            f"norm+rope+pack of q, k, v (S={s}, H={h}, D={D}, P={p})"
     raise SystemExit(f"unknown --kernel-only case {name!r}")
+
+
+def kernel_case_bytes(name: str) -> float:
+    """Algorithmic HBM bytes of a prologue case: read q, k, v once (bf16),
+    write the packed slabs once (P * Hg heads, padding included), read the
+    cos / sin tables once (float32, D/2 each per token); weights stay in L2."""
+    s, h, p = (int(x) for x in name.split(":")[1].split(","))
+    hg = -(-h // p)
+    return 3 * s * h * D * 2 + 3 * s * p * hg * D * 2 + 2 * s * (D // 2) * 4
 
 
 def run_kernel_only(args):
@@ -223,9 +249,13 @@ def run_kernel_only(args):
     fn, fl, desc = kernel_case(args.kernel_only, dev)
     ms = time_launches(fn, args.steps, args.warmup)
     assert _lib.device_status() == 0
-    print(json.dumps({"case": args.kernel_only, "desc": desc, "ms_per_launch": round(ms, 4),
-                      "tflops": round(fl / (ms / 1e3) / 1e12, 2), "launches": args.steps}),
-          flush=True)
+    rec = {"case": args.kernel_only, "desc": desc, "ms_per_launch": round(ms, 4)}
+    if args.kernel_only.startswith("prologue:"):
+        rec["gbs"] = round(kernel_case_bytes(args.kernel_only) / (ms / 1e3) / 1e9, 1)
+    else:
+        rec["tflops"] = round(fl / (ms / 1e3) / 1e12, 2)
+    rec["launches"] = args.steps
+    print(json.dumps(rec), flush=True)
 
 
 def run_reference(args, rank: int):
@@ -458,7 +488,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the extra cfg2 / cfg4 single-kernel measurements")
     ap.add_argument("--kernel-only", default=None,
-                    help="time one kernel case (cfg2, cfg4, attn:B,S,H, na3d:T,H,W,NH) and exit")
+                    help="time one kernel case (cfg2, cfg4, attn:B,S,H, na3d:T,H,W,NH, "
+                         "prologue:S,H,P) and exit")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

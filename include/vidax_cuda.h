@@ -115,6 +115,52 @@ int vx_ulysses_pack(const vx_head_slab_args* args, vx_stream_t stream);
 int vx_ulysses_unpack(const vx_head_slab_args* args, vx_stream_t stream);
 
 /* ----------------------------------------------------------------------
+ * Fused pre-attention step: RMSNorm + 3-D RoPE + head-slab pack, one HBM
+ * pass over q / k / v.
+ *
+ * Replaces, per layer, the sequence after the q/k/v projections in Wan's
+ * attention (src/vidax/models/wan/common/dit_layers.py:137-157):
+ * RMSNorm(dim) on q and k (src/vidax/core/attention.py:149-162), the reshape
+ * to (B, S, H, D), apply_rope3d (src/vidax/core/rope3d.py:89-111) and the
+ * tokens->heads packing of sequence_parallel_self_attention
+ * (attention.py:379-381). per_head = 1 gives RMSNorm(head_dim) of
+ * HunyuanVideo (hunyuan_video/common/dit_layers.py:358) and LTX-2.5's
+ * neighborhood attention (ltx2_5/diffusion_vae.py:263), whose q scaling
+ * (:265) is post_scale.
+ *
+ * Per tensor t (weight NULL: no norm; rope bit clear: no rotation; both, and
+ * post_scale 1: plain pack, e.g. v):
+ *   y = bf16(bf16(x * 1/sqrt(sum(x^2)/cols + eps)) * bf16(w))   cols = H*D or D
+ *   y = bf16(y * post_scale)                                    if != 1
+ *   (y[2p], y[2p+1]) -> (bf16(a c - b s), bf16(b c + a s)),  c, s = cos/sin[token][p]
+ *
+ * dst[t], per batch item b (item size groups * seq * hg * D elements,
+ * hg = ceil(heads / groups)), slice by slice j:
+ *   [j][g][s][i < slice_heads[j]][D]   with head = g * hg + slice_off[j] + i,
+ * zero for head >= heads. groups = 1, one slice: plain (B, seq, heads, D).
+ */
+typedef struct vx_norm_rope_pack_args {
+  int32_t num_tensors;          /* 1..3 */
+  const void* src[3];           /* bf16 rows, d contiguous */
+  void* dst[3];                 /* bf16, contiguous packed layout above */
+  int64_t src_stride[3][3];     /* element strides of (batch, seq, head); multiples of 8 */
+  const float* norm_weight[3];  /* H*D (per_head 0) or D (per_head 1) floats; NULL = no norm */
+  int32_t per_head;
+  float eps;
+  float post_scale[3];          /* 1.0 = none */
+  const float* rope_cos;        /* (seq, D/2) float tables, token-major; NULL = no RoPE */
+  const float* rope_sin;
+  int64_t rope_stride;          /* floats between consecutive tokens (multiple of 4, >= D/2) */
+  int32_t rope_mask;            /* bit t: rotate tensor t */
+  int32_t batch, seq, heads, head_dim;
+  int32_t groups;               /* destination head groups (Ulysses ranks); 1 = no regrouping */
+  int32_t num_slices;           /* 0 (one slice of hg heads) or 1..8 */
+  int32_t slice_heads[8];       /* heads per group in each slice; sum = hg */
+} vx_norm_rope_pack_args;
+
+int vx_norm_rope_pack(const vx_norm_rope_pack_args* args, vx_stream_t stream);
+
+/* ----------------------------------------------------------------------
  * 3-D neighborhood attention (NATTEN-style clamped windows, non-causal).
  *
  * Replaces vidax.models.ltx2_5.diffusion_vae.neighborhood_attention_3d

@@ -58,6 +58,35 @@ def main():
             same_txt = all(torch.equal(gathered[0][:, :T_len], g[:, :T_len]) for g in gathered)
             print(f"joint B={B} T={T_len} S={S} H={H}: max {mx:.3g} mean {mean:.3g} txt-replicated {same_txt}", flush=True)
             ok = ok and mx <= 2e-2 and mean <= 2e-3 and same_txt
+    # Wan attend: fused RMSNorm + RoPE + pack, then the Ulysses pipeline; each
+    # rank holds its chunk of the projections and of the RoPE tables
+    for (t, h, w, H) in [(4, 8, 16, 8), (2, 6, 16, 5)]:
+        S, D = t * h * w, 128
+        sl = S // world
+        q, k, v = seeded_qkv((1, S, H * D), 970 + S + H, head_scale_range=None)
+        rng = np.random.Generator(np.random.PCG64(S + H))
+        wq, wk = ((1.0 + 0.25 * rng.standard_normal(H * D)).astype(np.float32) for _ in range(2))
+        cos, sin = vx.rope3d_freqs(t, h, w, D)
+        full = [torch.from_numpy(np.ascontiguousarray(x)).cuda().bfloat16() for x in (q, k, v)]
+        mine = [x[:, rank * sl:(rank + 1) * sl] for x in full]
+        rope_mine = (cos[rank * sl:(rank + 1) * sl], sin[rank * sl:(rank + 1) * sl])
+        out = vx.attend(*mine, H, norm_q=torch.from_numpy(wq), norm_k=torch.from_numpy(wk),
+                        rope=rope_mine, sp_axis_name="sp")
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out.contiguous())
+        if rank == 0:
+            got = torch.cat(gathered, dim=1)
+            single = vx.attend(*full, H, norm_q=torch.from_numpy(wq), norm_k=torch.from_numpy(wk),
+                               rope=(cos, sin))
+            same = torch.equal(got, single)
+            from oracle.rope_norm_ref import norm_rope
+            qr = norm_rope(q, wq, cos.numpy(), sin.numpy(), H)
+            kr = norm_rope(k, wk, cos.numpy(), sin.numpy(), H)
+            ref = sdpa(qr, kr, v.reshape(1, S, H, D))
+            mx, mean = compare(got.float().cpu().numpy().reshape(1, S, H, D), ref)
+            print(f"attend S={S} H={H}: max {mx:.3g} mean {mean:.3g} equals-single-gpu {same}",
+                  flush=True)
+            ok = ok and mx <= 2e-2 and mean <= 2e-3 and same
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.broadcast(flag, 0)
     vx.unregister_axis("sp")

@@ -10,7 +10,11 @@ in a namespace where `jax` / `jnp` are a small numpy shim:
 * src/vidax/core/attention.py: `chunk_by_rank`, `local_attention`,
   `dot_product_attention`, `sequence_parallel_self_attention` (lines
   132-146, 321-388, 467-533), run on P threads (one per emulated device)
-  whose `jax.lax.all_to_all` / `axis_index` meet at a barrier.
+  whose `jax.lax.all_to_all` / `axis_index` meet at a barrier;
+* src/vidax/core/rope3d.py: `_axis_freqs`, `create_rope3d_freqs`,
+  `apply_rope3d` (lines 33-111);
+* src/vidax/core/attention.py: `RMSNorm.__call__` (lines 149-162), run as a
+  plain function on a stand-in module object.
 
 The shim restates the third-party jax primitives the code calls: `jnp.take`,
 `jnp.moveaxis`, `jnp.einsum` (bf16 operands, f32 accumulation, result in the
@@ -236,6 +240,72 @@ def gen_attention():
     return out
 
 
+def gen_rope():
+    """create_rope3d_freqs / apply_rope3d (src/vidax/core/rope3d.py) on small grids."""
+    ns = make_namespace()
+    jnp = ns["jnp"]
+    jnp.power = np.power
+    jnp.outer = np.outer
+    jnp.cos = np.cos
+    jnp.sin = np.sin
+    jnp.stack = np.stack
+    ns["Tuple"] = tuple
+    load_functions("src/vidax/core/rope3d.py", ["_axis_freqs", "create_rope3d_freqs", "apply_rope3d"], ns)
+    out = {}
+    for i, (t, h, w, hd) in enumerate([(3, 4, 5, 128), (2, 3, 7, 64)]):
+        cos, sin = ns["create_rope3d_freqs"](t, h, w, hd)
+        x = seeded((1, t * h * w, 3, hd), 120 + i)
+        y = ns["apply_rope3d"](x, (np.asarray(cos), np.asarray(sin)))
+        assert y.dtype == BF16
+        out[f"rope{i}_grid"] = np.array([t, h, w, hd], np.int32)
+        out[f"rope{i}_cos"] = np.asarray(cos, np.float32)[0, :, 0, :]
+        out[f"rope{i}_sin"] = np.asarray(sin, np.float32)[0, :, 0, :]
+        out[f"rope{i}_x"] = x.astype(np.float32)
+        out[f"rope{i}_y"] = y.astype(np.float32)
+    return out
+
+
+def load_method(relpath, cls, name, ns):
+    """Executes method `name` of class `cls` as a plain function (first
+    argument `self`); decorators such as nn.compact are dropped."""
+    import textwrap
+    path = os.path.join(REF, relpath)
+    src = open(path).read()
+    for node in ast.parse(src).body:
+        if isinstance(node, ast.ClassDef) and node.name == cls:
+            for fn in node.body:
+                if isinstance(fn, ast.FunctionDef) and fn.name == name:
+                    seg = textwrap.dedent(ast.get_source_segment(src, fn))
+                    exec(compile("\n" * (fn.lineno - 1) + seg, path, "exec"), ns)
+                    return ns[name]
+    raise RuntimeError(f"{cls}.{name} not found in {path}")
+
+
+def gen_rmsnorm():
+    """RMSNorm.__call__ (src/vidax/core/attention.py:149-162): full-row (Wan)
+    and per-head (HunyuanVideo / LTX-2.5) widths. jax.lax.rsqrt is shimmed as
+    float32 1/sqrt; the fixture pins where the float32 / bf16 casts sit."""
+    ns = make_namespace()
+    jnp = ns["jnp"]
+    jnp.mean = np.mean
+    jnp.square = np.square
+    ns["jax"].lax.rsqrt = lambda v: (np.float32(1.0) / np.sqrt(v)).astype(np.float32)
+    ns["nn"] = types.SimpleNamespace(initializers=types.SimpleNamespace(ones=None))
+    call = load_method("src/vidax/core/attention.py", "RMSNorm", "__call__", ns)
+    out = {}
+    for i, (rows, dim) in enumerate([(37, 1536), (29, 5120), (41, 128), (23, 64)]):
+        rng = np.random.Generator(np.random.PCG64(140 + i))
+        w = (1.0 + 0.25 * rng.standard_normal(dim)).astype(np.float32)
+        x = seeded((rows, dim), 150 + i, scale=3.0)
+        module = types.SimpleNamespace(dim=dim, eps=1e-6, param=lambda name, init, shape, w=w: w)
+        y = call(module, x)
+        assert y.dtype == BF16
+        out[f"rms{i}_x"] = x.astype(np.float32)
+        out[f"rms{i}_w"] = w
+        out[f"rms{i}_y"] = y.astype(np.float32)
+    return out
+
+
 def main():
     if not REF or not os.path.isdir(REF):
         sys.exit("usage: make_golden.py <path-to-vidax-checkout>")
@@ -243,7 +313,10 @@ def main():
     np.savez_compressed(os.path.join(OUT_DIR, "na3d_reference.npz"), **na)
     at = gen_attention()
     np.savez_compressed(os.path.join(OUT_DIR, "attention_reference.npz"), **at)
-    for f in ("na3d_reference.npz", "attention_reference.npz"):
+    ro = gen_rope()
+    ro.update(gen_rmsnorm())
+    np.savez_compressed(os.path.join(OUT_DIR, "rope_reference.npz"), **ro)
+    for f in ("na3d_reference.npz", "attention_reference.npz", "rope_reference.npz"):
         print(f, os.path.getsize(os.path.join(OUT_DIR, f)), "bytes")
 
 

@@ -75,3 +75,27 @@ def test_pack_validation(lib):
     assert fn(ctypes.byref(a), None) == _lib.VX_EINVAL
     a.num_tensors, a.seq, a.heads, a.head_dim, a.groups = 1, 4, 4, 96, 2
     assert fn(ctypes.byref(a), None) == _lib.VX_EUNSUPPORTED
+
+
+def test_norm_rope_pack_validation_without_device(lib):
+    from vidax_b200 import _lib
+    from vidax_b200.prologue import NormRopePackArgs
+    assert lib.vx_norm_rope_pack(None, None) == _lib.VX_EINVAL
+    a = NormRopePackArgs()
+    a.num_tensors, a.batch, a.seq, a.heads, a.head_dim, a.groups = 1, 1, 4, 2, 96, 1
+    assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_EUNSUPPORTED
+    a.head_dim = 128
+    a.heads = 65   # 8320 features: above the 8192 a warp holds
+    assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_EUNSUPPORTED
+    a.heads, a.groups, a.num_slices = 5, 2, 2
+    a.slice_heads[0], a.slice_heads[1] = 1, 1        # sums to 2, ceil(5 / 2) = 3
+    assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_EINVAL
+    assert b"slice_heads" in lib.vx_last_error()
+    a.slice_heads[1] = 2
+    a.rope_mask = 1                                  # rotation without tables
+    assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_EINVAL
+    a.rope_mask = 0
+    assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_EINVAL  # NULL src/dst
+    a.seq = 0
+    a.src[0] = a.dst[0] = 4096
+    assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_OK     # empty: no launch

@@ -95,3 +95,22 @@ def test_all_to_all_tiled_is_inverse_of_itself():
     back = all_to_all_tiled(there, 1, 2)
     for a, b in zip(xs, back):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("i", [0, 1])
+def test_rope_oracle_matches_reference_code(i):
+    from oracle.rope_norm_ref import apply_rope3d, rope3d_freqs
+    g = np.load(os.path.join(GOLDEN, "rope_reference.npz"))
+    t, h, w, hd = (int(x) for x in g[f"rope{i}_grid"])
+    cos, sin = rope3d_freqs(t, h, w, hd)
+    assert np.array_equal(cos, g[f"rope{i}_cos"]) and np.array_equal(sin, g[f"rope{i}_sin"])
+    y = apply_rope3d(g[f"rope{i}_x"], cos, sin)
+    assert np.array_equal(y, g[f"rope{i}_y"])
+
+
+@pytest.mark.parametrize("i", [0, 1, 2, 3])
+def test_rmsnorm_oracle_matches_reference_code(i):
+    from oracle.rope_norm_ref import rms_norm
+    g = np.load(os.path.join(GOLDEN, "rope_reference.npz"))
+    y = rms_norm(g[f"rms{i}_x"], g[f"rms{i}_w"])
+    assert np.array_equal(y, g[f"rms{i}_y"])

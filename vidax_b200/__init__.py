@@ -20,6 +20,7 @@ from .attention import (  # noqa: F401
 )
 from .hostio import attention_from_host  # noqa: F401
 from .neighborhood import na3d_flops, neighborhood_attention_3d  # noqa: F401
+from .prologue import attend, norm_rope_pack, rms_norm_rope, rope3d_freqs  # noqa: F401
 from .ulysses import (  # noqa: F401
     axis_index,
     axis_size,

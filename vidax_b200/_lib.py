@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "vx_na3d_window_start",
     "vx_ulysses_pack",
     "vx_ulysses_unpack",
+    "vx_norm_rope_pack",
     "vx_memcpy_rows_async",
     "vx_selftest_wait_timeout",
 )

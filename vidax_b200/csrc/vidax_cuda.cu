@@ -19,6 +19,7 @@
 #include <utility>
 
 #include "attn_sm100.cuh"
+#include "norm_rope_pack.cuh"
 #include "ulysses_pack.cuh"
 
 namespace {
@@ -600,6 +601,105 @@ extern "C" int vx_memcpy_rows_async(void* dst, int64_t dst_pitch, const void* sr
                                     static_cast<size_t>(rows), cudaMemcpyDefault,
                                     reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
+  return VX_OK;
+}
+
+extern "C" int vx_norm_rope_pack(const vx_norm_rope_pack_args* a, vx_stream_t stream) {
+  using namespace vx::prologue;
+  if (a == nullptr) return fail(VX_EINVAL, "args is NULL");
+  if (a->num_tensors < 1 || a->num_tensors > 3)
+    return fail(VX_EINVAL, "num_tensors must be 1..3 (got %d)", a->num_tensors);
+  if (a->batch < 0 || a->seq < 0 || a->heads <= 0 || a->groups <= 0)
+    return fail(VX_EINVAL, "bad sizes (batch=%d seq=%d heads=%d groups=%d)", a->batch, a->seq,
+                a->heads, a->groups);
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return fail(VX_EUNSUPPORTED, "head_dim %d (64, 128 or 256)", a->head_dim);
+  const int vpd = a->head_dim / 8;
+  const long long row_vecs = static_cast<long long>(a->heads) * vpd;
+  if (row_vecs > 32 * 32)
+    return fail(VX_EUNSUPPORTED, "heads * head_dim = %lld (at most 8192 features per token)",
+                row_vecs * 8);
+  if (a->per_head != 0 && a->per_head != 1) return fail(VX_EINVAL, "per_head must be 0 or 1");
+  if (!(a->eps >= 0.f)) return fail(VX_EINVAL, "eps must be >= 0");
+  NormRopeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.num_tensors = a->num_tensors;
+  p.batch = a->batch;
+  p.seq = a->seq;
+  p.heads = a->heads;
+  p.vpd_log2 = vpd == 8 ? 3 : (vpd == 16 ? 4 : 5);
+  p.per_head = a->per_head;
+  p.eps = a->eps;
+  p.cols = static_cast<float>(a->per_head ? a->head_dim : a->heads * a->head_dim);
+  p.groups = a->groups;
+  p.hg = (a->heads + a->groups - 1) / a->groups;
+  const int ns = a->num_slices == 0 ? 1 : a->num_slices;
+  if (ns < 1 || ns > kMaxSlices) return fail(VX_EINVAL, "num_slices must be 0..%d", kMaxSlices);
+  p.num_slices = ns;
+  p.slice_off[0] = 0;
+  if (a->num_slices == 0) {
+    p.slice_off[1] = p.hg;
+  } else {
+    for (int j = 0; j < ns; ++j) {
+      if (a->slice_heads[j] <= 0) return fail(VX_EINVAL, "slice_heads[%d] must be > 0", j);
+      p.slice_off[j + 1] = p.slice_off[j] + a->slice_heads[j];
+    }
+    if (p.slice_off[ns] != p.hg)
+      return fail(VX_EINVAL, "slice_heads sum to %d, expected ceil(heads / groups) = %d",
+                  p.slice_off[ns], p.hg);
+  }
+  for (int j = ns + 1; j <= kMaxSlices; ++j) p.slice_off[j] = p.hg;
+  p.item_vecs = static_cast<long long>(a->groups) * a->seq * p.hg * vpd;
+  p.rope_mask = a->rope_mask & ((1 << a->num_tensors) - 1);
+  if (p.rope_mask != 0) {
+    if (a->rope_cos == nullptr || a->rope_sin == nullptr)
+      return fail(VX_EINVAL, "rope_mask set but rope tables are NULL");
+    if (!aligned16(a->rope_cos) || !aligned16(a->rope_sin))
+      return fail(VX_EINVAL, "rope tables must be 16-byte aligned");
+    if (a->rope_stride < a->head_dim / 2 || a->rope_stride % 4 != 0)
+      return fail(VX_EINVAL, "rope_stride %lld (multiple of 4, >= head_dim / 2)",
+                  (long long)a->rope_stride);
+    p.cos = a->rope_cos;
+    p.sin = a->rope_sin;
+    p.rope_stride = a->rope_stride;
+  }
+  for (int t = 0; t < a->num_tensors; ++t) {
+    if (a->src[t] == nullptr || a->dst[t] == nullptr)
+      return fail(VX_EINVAL, "tensor %d: NULL pointer", t);
+    if (!aligned16(a->src[t]) || !aligned16(a->dst[t]))
+      return fail(VX_EINVAL, "tensor %d: pointers must be 16-byte aligned", t);
+    for (int k = 0; k < 3; ++k)
+      if (a->src_stride[t][k] < 0 || a->src_stride[t][k] % 8 != 0)
+        return fail(VX_EINVAL, "tensor %d: strides must be non-negative multiples of 8", t);
+    if (a->norm_weight[t] != nullptr && !aligned16(a->norm_weight[t]))
+      return fail(VX_EINVAL, "tensor %d: norm weight must be 16-byte aligned", t);
+    if (!std::isfinite(a->post_scale[t]))
+      return fail(VX_EINVAL, "tensor %d: post_scale must be finite", t);
+    p.src[t] = static_cast<const uint4*>(a->src[t]);
+    p.dst[t] = static_cast<uint4*>(a->dst[t]);
+    p.b_stride[t] = a->src_stride[t][0] / 8;
+    p.s_stride[t] = a->src_stride[t][1] / 8;
+    p.h_stride[t] = a->src_stride[t][2] / 8;
+    p.weight[t] = a->norm_weight[t];
+    p.post_scale[t] = a->post_scale[t];
+  }
+  const long long rows = static_cast<long long>(a->batch) * a->seq;
+  if (rows == 0) return VX_OK;
+  const long long blocks = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+  if (blocks > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "too many rows");
+  dim3 grid(static_cast<unsigned>(blocks), a->num_tensors);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long per_lane = (row_vecs + 31) / 32;
+  if (per_lane <= 8)
+    norm_rope_pack_kernel<8><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
+  else if (per_lane <= 16)
+    norm_rope_pack_kernel<16><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
+  else if (per_lane <= 24)
+    norm_rope_pack_kernel<24><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
+  else
+    norm_rope_pack_kernel<32><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "norm_rope_pack launch");
   return VX_OK;
 }
 

@@ -188,24 +188,31 @@ def _timed_attention(q, k, v, sm_scale, kv_len, out):
     return o
 
 
-def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int]):
+def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optional[int],
+                 sends=None):
     """One batch item: qb/kb/vb/ob are (S_loc, H, D) views.
 
     The rank's head group (Hg heads after the exchange) is split into slices
     (`_pieces`); slice j+1's three tokens->heads all-to-alls run on NCCL's
     stream while the kernel computes slice j, and slice j's heads->tokens
-    all-to-all and unpack (on a side stream) overlap the kernel on slice j+1."""
-    S_loc, H, D = qb.shape
+    all-to-all and unpack (on a side stream) overlap the kernel on slice j+1.
+    `sends` (per slice, [q, k, v] of (P, S_loc, hs, D)) replaces the packing
+    of qb/kb/vb when the send slabs were already written by the fused
+    norm + RoPE + pack kernel."""
+    S_loc, H, D = ob.shape
     Hg = -(-H // P)
     S = P * S_loc
     kv_len = None
     if kv_valid is not None and kv_valid < S:
-        kv_len = torch.full((1,), kv_valid, dtype=torch.int32, device=qb.device)
+        kv_len = torch.full((1,), kv_valid, dtype=torch.int32, device=ob.device)
     sizes = _pieces(Hg)
     offs = [sum(sizes[:j]) for j in range(len(sizes))]
     subs = [(hs, Hg, off, hs) for hs, off in zip(sizes, offs)]
     n = len(subs)
-    sends = [pack_heads([qb, kb, vb], P, sub=sub) for sub in subs]   # each (P, S_loc, hs, D)
+    if sends is None:
+        sends = [pack_heads([qb, kb, vb], P, sub=sub) for sub in subs]   # each (P, S_loc, hs, D)
+    else:
+        sends = list(sends)
     recvs, works = [None] * n, [None] * n
 
     def start_in(j):
@@ -213,8 +220,8 @@ def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optio
         works[j] = [dist.all_to_all_single(r, t, group=group, async_op=True)
                     for r, t in zip(recvs[j], sends[j])]
 
-    comp = torch.cuda.current_stream(qb.device)
-    side = _side_stream(qb.device)
+    comp = torch.cuda.current_stream(ob.device)
+    side = _side_stream(ob.device)
     side.wait_stream(comp)
     start_in(0)
     for j, sub in enumerate(subs):
@@ -265,6 +272,29 @@ def sequence_parallel_self_attention(
     for b in range(q.shape[0]):
         _ulysses_one(q[b], k[b], v[b], out[b], group, P, sm_scale, valid_len)
     return out
+
+
+def _attend_sp(q, k, v, num_heads, norm_q, norm_k, rope, eps, sp_axis_name, scale):
+    """Wan's attend under sequence parallelism (dit_layers.py:137-151): one
+    fused norm + RoPE + pack launch writes every pipelined slice's send slabs
+    for all batch items, then the Ulysses exchange / attention pipeline."""
+    from .prologue import norm_rope_pack, slice_views
+    group = _group(sp_axis_name)
+    P = dist.get_world_size(group)
+    B, L, dim = q.shape
+    H = num_heads
+    D = dim // H
+    sizes = _pieces(-(-H // P))
+    bufs = norm_rope_pack([q, k, v], H, norm_weights=[norm_q, norm_k, None], eps=eps,
+                          rope=rope, rope_mask=0b011 if rope is not None else 0,
+                          groups=P, slices=sizes)
+    out = torch.empty((B, L, H, D), dtype=q.dtype, device=q.device)
+    sm_scale = D ** -0.5 if scale is None else scale
+    for b in range(B):
+        per_t = [slice_views(buf[b], P, L, D, sizes) for buf in bufs]
+        sends = [[per_t[t][j] for t in range(3)] for j in range(len(sizes))]
+        _ulysses_one(None, None, None, out[b], group, P, sm_scale, None, sends=sends)
+    return out.reshape(B, L, dim)
 
 
 def sequence_parallel_joint_self_attention(
