@@ -165,3 +165,66 @@ def test_attend_matches_oracle():
     ref = sdpa(qr, kr, v.reshape(1, S, heads, D))
     mx, mean = compare(got.float().cpu().numpy().reshape(1, S, heads, D), ref)
     assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)
+
+
+def _call_raw(srcs, dsts, heads, D, weights, tables, rope_stride, groups=1):
+    """vx_norm_rope_pack with explicit table pointers / strides (the Python
+    wrapper always pairs the tables)."""
+    import ctypes
+    from vidax_b200 import _lib
+    from vidax_b200.prologue import NormRopePackArgs
+    a = NormRopePackArgs()
+    a.num_tensors = len(srcs)
+    for i, (x, o) in enumerate(zip(srcs, dsts)):
+        a.src[i], a.dst[i] = x.data_ptr(), o.data_ptr()
+        for k in range(3):
+            a.src_stride[i][k] = x.stride(k)
+        if weights[i] is not None:
+            a.norm_weight[i] = weights[i].data_ptr()
+        a.post_scale[i] = 1.0
+    a.eps = 1e-6
+    a.rope_cos, a.rope_sin = tables[0].data_ptr(), tables[1].data_ptr()
+    a.rope_stride = rope_stride
+    a.rope_mask = 0b011
+    a.batch, a.seq, a.heads, a.head_dim, a.groups = srcs[0].shape[0], srcs[0].shape[1], heads, D, groups
+    lib = _lib.load()
+    stream = torch.cuda.current_stream()
+    _lib.check(lib.vx_norm_rope_pack(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layout", ["fused_qkv", "strided_heads", "plain"])
+@pytest.mark.parametrize("tables", ["separate", "paired_padded", "paired"])
+def test_source_and_table_layouts(layout, tables):
+    """Every source-copy form (tokens adjacent, rows adjacent only, heads
+    strided) and table form (separate cos / sin, cos|sin rows with padding,
+    packed cos|sin rows) gives the same bits."""
+    from vidax_b200 import norm_rope_pack
+    H, D, S, B = 6, 128, 77, 2
+    base = [_cuda(_seeded((B, S, H, D), 80 + i, scale=2.0)) for i in range(3)]
+    w = [torch.from_numpy(_weight(H * D, 90 + i)).cuda() for i in range(2)] + [None]
+    ang = np.random.Generator(np.random.PCG64(3)).uniform(-20, 20, (S, D // 2)).astype(np.float32)
+    cos, sin = torch.from_numpy(np.cos(ang)).cuda(), torch.from_numpy(np.sin(ang)).cuda()
+    want = norm_rope_pack(base, H, norm_weights=w, rope=(cos, sin))
+    if layout == "fused_qkv":      # (B, S, 3, H, D) buffer: tokens 3*H*D apart
+        buf = torch.stack(base, dim=2)
+        srcs = [buf[:, :, i] for i in range(3)]
+    elif layout == "strided_heads":  # (B, S, H, 3, D): heads 3*D apart
+        buf = torch.stack(base, dim=3)
+        srcs = [buf[:, :, :, i] for i in range(3)]
+    else:
+        srcs = base
+    if tables == "separate":
+        tabs, stride = (cos.contiguous(), sin.contiguous()), D // 2
+    elif tables == "paired_padded":  # rows [cos | sin | pad]
+        both = torch.zeros((S, 2 * D), device="cuda")
+        both[:, :D // 2], both[:, D // 2:D] = cos, sin
+        tabs, stride = (both[:, :D // 2], both[:, D // 2:D]), 2 * D
+    else:
+        both = torch.cat([cos, sin], dim=1)
+        tabs, stride = (both[:, :D // 2], both[:, D // 2:]), D
+    got = [torch.empty_like(x) for x in want]
+    _call_raw(srcs, got, H, D, w, tabs, stride)
+    torch.cuda.synchronize()
+    for g_, w_ in zip(got, want):
+        assert torch.equal(g_, w_)

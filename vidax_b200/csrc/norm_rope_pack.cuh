@@ -24,10 +24,27 @@
 //   rope  : (a, b) -> (bf16(a c - b s), bf16(b c + a s)) on adjacent pairs,
 //           products and sums each rounded in float32 (no FMA contraction).
 //
-// Layout: one warp per (token row, tensor). Lane l holds the 16-byte vectors
-// v = 32 i + l of the row (8 bf16 each), so a head of D elements sits in
-// D/8 consecutive lanes and per-head sums reduce with xor shuffles inside that
-// lane segment. Output per tensor and batch item, slice by slice:
+// Layout: a persistent CTA (one per SM) streams work items -- R consecutive
+// tokens of one tensor -- through a ring of shared-memory stages. Lanes 0-3
+// of warp 0 are the producer: in lockstep, each waits for the stage of its
+// own item and fills it with untiled bulk copies (one for the R rows when the
+// tokens are adjacent in memory, else one per row or per head) plus, for
+// rotated tensors, the tokens' cos / sin rows into a table slot of the same
+// index (one copy when the cos and sin rows are interleaved per token). Four
+// lanes keep four fills in flight per issue round; one thread alone issues
+// one copy per ~400 cycles, too few for HBM rates with small rows.
+//
+// Warps 1..8 are consumers, each owning whole items (item n of the CTA goes to
+// warp n % 8; the ring depth is a multiple of 8, so stage n % S is waited on
+// by one warp only, one phase at a time). Per row, lane l handles the 16-byte
+// vectors v = l + 32 i (8 bf16 each) in rolled loops that read the stage:
+// pass 1 sums x^2, pass 2 transforms and stores. A head of D elements is D/8
+// consecutive lanes, so per-head sums reduce with xor shuffles inside that
+// lane segment. Rolled loops keep the code small (the fully unrolled form
+// stalled on instruction fetch). Destination offsets come from a per-CTA head
+// table (slice, group and position of every head), built once.
+//
+// Output per tensor and batch item, slice by slice:
 //   [slice j][group g][token s][head i < slice_heads[j]][d]
 // with zero heads past H (padding when H % G != 0).
 #pragma once
@@ -40,7 +57,18 @@ namespace vx {
 namespace prologue {
 
 constexpr int kMaxSlices = 8;
-constexpr int kWarpsPerCta = 4;
+constexpr int kConsumerWarps = 8;
+constexpr int kProducerLanes = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kMaxStages = 32;      // a multiple of kConsumerWarps
+constexpr int kMinStages = 16;      // 8 held by consumers + at least 8 in flight
+constexpr int kStageAlign = 128;
+constexpr int kTargetStageBytes = 10 * 1024;  // rows per stage: R = max(1, this / row bytes)
+constexpr int kMaxRowsPerStage = 8;
+constexpr int kMaxHeadSlots = 512;  // groups * ceil(heads / groups)
+// Shared memory of one CTA (one CTA per SM): weights, head table, row ring,
+// table ring, control.
+constexpr int kSmemBudget = 200 * 1024;
 
 struct NormRopeParams {
   const uint4* src[3];
@@ -61,6 +89,34 @@ struct NormRopeParams {
   int num_slices;
   int slice_off[kMaxSlices + 1];  // prefix sums of the slices' heads; slice_off[num_slices] = hg
   long long item_vecs;            // packed 16-byte vectors per tensor and batch item
+  int rows_per_stage;             // R
+  int blocks;                     // ceil(seq / R) token blocks per batch item
+  int items;                      // num_tensors * batch * blocks
+  int stages;                     // ring depth, a multiple of kConsumerWarps
+  int stage_bytes;                // R rows, rounded up to kStageAlign
+  int row_bytes;                  // heads * D * 2
+  int table_bytes;                // cos and sin rows of R tokens (R * D * 4), 0 without RoPE
+  int contiguous[3];              // 1: heads adjacent, 2: and tokens adjacent (one copy)
+  int table_mode;                 // 2: cos|sin interleaved per token, tokens adjacent;
+                                  // 1: interleaved per token; 0: separate tables
+  int weight_off[3];              // shared-memory offset of tensor t's bf16 weights (-1: none)
+  int head_off;                   // shared-memory offset of the head table
+  int ring_off;                   // shared-memory offset of the row ring
+  int table_off;                  // shared-memory offset of the table ring
+  int ctl_off;                    // shared-memory offset of RingControl
+};
+
+// Destination of head slot h (h < groups * hg) for token 0 of a batch item,
+// and the distance between consecutive tokens, both in 16-byte vectors.
+struct HeadSlot {
+  long long base;
+  long long token_stride;
+};
+
+struct RingControl {
+  uint64_t full[kMaxStages];   // rows (and tables) of item n landed in stage n % stages
+  uint64_t empty[kMaxStages];  // stage n % stages consumed
+  int abort_flag;
 };
 
 __device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
@@ -68,10 +124,10 @@ __device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u 
 __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
+// Two floats -> packed bf16x2 (round to nearest even), one conversion.
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-  const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-  return l | (h << 16);
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 __device__ __forceinline__ void unpack8(const uint4& x, float f[8]) {
@@ -87,131 +143,279 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
   return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
 }
 
-// Packed 16-byte vector index (within one batch item) of head h's vector dv
-// of token s.
-__device__ __forceinline__ long long packed_index(const NormRopeParams& p, int s, int h, int dv) {
+__device__ __forceinline__ HeadSlot head_slot(const NormRopeParams& p, int h) {
   const int g = h / p.hg;
   const int i = h - g * p.hg;
   int j = 0;
-#pragma unroll
-  for (int k = 1; k < kMaxSlices; ++k)
-    if (k < p.num_slices && i >= p.slice_off[k]) j = k;
+  for (int k = 1; k < p.num_slices; ++k)
+    if (i >= p.slice_off[k]) j = k;
   const int off = p.slice_off[j];
   const int hs = p.slice_off[j + 1] - off;
-  const long long base = static_cast<long long>(p.groups) * p.seq * off;  // slice start, in head rows
-  const long long row = base + (static_cast<long long>(g) * p.seq + s) * hs + (i - off);
-  return (row << p.vpd_log2) + dv;
+  // slice j starts at groups * seq * off head rows; group g of it at g * seq * hs
+  const long long row0 = static_cast<long long>(p.groups) * p.seq * off +
+                         static_cast<long long>(g) * p.seq * hs + (i - off);
+  HeadSlot slot;
+  slot.base = row0 << p.vpd_log2;
+  slot.token_stride = static_cast<long long>(hs) << p.vpd_log2;
+  return slot;
 }
 
-// kV: 16-byte vectors held per lane (rows of up to 32 * kV * 8 features).
-template <int kV>
-__global__ void __launch_bounds__(kWarpsPerCta * 32) norm_rope_pack_kernel(
-    const __grid_constant__ NormRopeParams p) {
-  const int t = blockIdx.y;
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-  if (row >= static_cast<long long>(p.batch) * p.seq) return;
-  const int b = static_cast<int>(row / p.seq);
-  const int s = static_cast<int>(row - static_cast<long long>(b) * p.seq);
-  const int dmask = (1 << p.vpd_log2) - 1;
-  const int nvec = p.heads << p.vpd_log2;
-  const uint4* __restrict__ src = p.src[t] + b * p.b_stride[t] + s * p.s_stride[t];
-  const long long hstr = p.h_stride[t];
+// item -> tensor t, batch item b, first token s0 and token count
+__device__ __forceinline__ void item_coords(const NormRopeParams& p, int item, int& t, int& b,
+                                            int& s0, int& count) {
+  const int blk = item / p.num_tensors;
+  t = item - blk * p.num_tensors;
+  b = blk / p.blocks;
+  s0 = (blk - b * p.blocks) * p.rows_per_stage;
+  count = min(p.rows_per_stage, p.seq - s0);
+}
 
-  uint4 x[kV];
+__device__ __forceinline__ float rms_inverse(float sumsq, float cols, float eps) {
+  const float var = __fdiv_rn(sumsq, cols);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
+__device__ __forceinline__ float sumsq8(const uint4& x) {
+  float f[8];
+  unpack8(x, f);
+  float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < kV; ++i) {
-    const int v = i * 32 + lane;
-    x[i] = make_uint4(0, 0, 0, 0);
-    if (v < nvec) x[i] = __ldg(src + (v >> p.vpd_log2) * hstr + (v & dmask));
+  for (int k = 0; k < 8; ++k) acc = fmaf(f[k], f[k], acc);
+  return acc;
+}
+
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// One 16-byte vector (8 features, pairs 4 dv .. 4 dv + 3): norm (r = 1/rms,
+// wv = 8 bf16 weights), post scale, rotation by the 4 (cos, sin) pairs c / sv.
+__device__ __forceinline__ uint4 transform8(const uint4& xin, bool norm, float r, const uint4 wv,
+                                            float ps, bool rope, const float4 c, const float4 sv) {
+  uint4 y = xin;
+  if (norm) {
+    float f[8];
+    unpack8(xin, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] = __fmul_rn(f[k], r);
+    // bf16 x bf16 products are exact in float32: one rounding, as the
+    // reference's bf16 multiply
+    y = make_uint4(mul_bf16x2(pack2(f[0], f[1]), wv.x), mul_bf16x2(pack2(f[2], f[3]), wv.y),
+                   mul_bf16x2(pack2(f[4], f[5]), wv.z), mul_bf16x2(pack2(f[6], f[7]), wv.w));
+  }
+  if (ps != 1.0f || rope) {
+    float f[8];
+    unpack8(y, f);
+    if (ps != 1.0f) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = round_bf16(__fmul_rn(f[k], ps));
+    }
+    if (rope) {
+      const float cc[4] = {c.x, c.y, c.z, c.w};
+      const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = f[2 * k], bb = f[2 * k + 1];
+        f[2 * k] = __fsub_rn(__fmul_rn(a, cc[k]), __fmul_rn(bb, ss[k]));
+        f[2 * k + 1] = __fadd_rn(__fmul_rn(bb, cc[k]), __fmul_rn(a, ss[k]));
+      }
+    }
+    y = pack8(f);
+  }
+  return y;
+}
+
+// Issues the bulk copies of item `item` into stage `stage` (producer lane).
+__device__ __forceinline__ void fill_stage(const NormRopeParams& p, uint8_t* smem, int item,
+                                           int stage, uint32_t full, uint64_t policy) {
+  int t, b, s0, count;
+  item_coords(p, item, t, b, s0, count);
+  const bool rope = (p.rope_mask >> t) & 1;
+  const uint32_t head_bytes = 16u << p.vpd_log2;  // D bf16
+  const uint32_t tok_table = 32u << p.vpd_log2;   // cos + sin of one token: D floats
+  mbar_expect_tx(full, count * p.row_bytes + (rope ? count * tok_table : 0));
+  const uint32_t dst = smem_u32(smem + p.ring_off + stage * p.stage_bytes);
+  const uint4* src = p.src[t] + b * p.b_stride[t] + s0 * p.s_stride[t];
+  if (p.contiguous[t] == 2) {
+    bulk_load(dst, src, count * p.row_bytes, full, policy);
+  } else {
+    for (int r = 0; r < count; ++r) {
+      const uint4* row = src + r * p.s_stride[t];
+      const uint32_t rdst = dst + r * p.row_bytes;
+      if (p.contiguous[t] == 1) {
+        bulk_load(rdst, row, p.row_bytes, full, policy);
+      } else {
+        for (int h = 0; h < p.heads; ++h)
+          bulk_load(rdst + h * head_bytes, row + h * p.h_stride[t], head_bytes, full, policy);
+      }
+    }
+  }
+  if (rope) {
+    const uint32_t tdst = smem_u32(smem + p.table_off + stage * p.table_bytes);
+    const float* cs = p.cos + s0 * p.rope_stride;
+    if (p.table_mode == 2) {
+      bulk_load(tdst, cs, count * tok_table, full, policy);
+    } else {
+      for (int r = 0; r < count; ++r) {
+        if (p.table_mode == 1) {
+          bulk_load(tdst + r * tok_table, cs + r * p.rope_stride, tok_table, full, policy);
+        } else {
+          bulk_load(tdst + r * tok_table, cs + r * p.rope_stride, tok_table / 2, full, policy);
+          bulk_load(tdst + r * tok_table + tok_table / 2, p.sin + (s0 + r) * p.rope_stride,
+                    tok_table / 2, full, policy);
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) norm_rope_pack_kernel(
+    const __grid_constant__ NormRopeParams p, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  RingControl& ctl = *reinterpret_cast<RingControl*>(smem + p.ctl_off);
+  const HeadSlot* slots = reinterpret_cast<const HeadSlot*>(smem + p.head_off);
+  const int S = p.stages;
+  const int nslots = p.groups * p.hg;
+  // norm weights, rounded to bf16 once (the reference multiplies by
+  // scale.astype(bf16)); destination head table
+  const int ncols = static_cast<int>(p.cols);
+  for (int t = 0; t < p.num_tensors; ++t) {
+    if (p.weight_off[t] < 0) continue;
+    uint32_t* wdst = reinterpret_cast<uint32_t*>(smem + p.weight_off[t]);
+    const float2* wsrc = reinterpret_cast<const float2*>(p.weight[t]);
+    for (int i = threadIdx.x; i < ncols / 2; i += kThreads) {
+      const float2 w2 = __ldg(wsrc + i);
+      wdst[i] = pack2(w2.x, w2.y);
+    }
+  }
+  for (int h = threadIdx.x; h < nslots; h += kThreads)
+    reinterpret_cast<HeadSlot*>(smem + p.head_off)[h] = head_slot(p, h);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&ctl.full[i]), 1);
+      mbar_init(smem_u32(&ctl.empty[i]), 1);
+    }
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &ctl.abort_flag;
+  const int G = gridDim.x;
+
+  if (threadIdx.x < 32) {
+    // ---------------------------------------------------------------- producer
+    const int lane = threadIdx.x;
+    if (lane >= kProducerLanes) return;
+    const uint64_t policy = l2_policy_evict_first();
+    int issued = 0;  // this lane's items issued: n = lane + kProducerLanes * k, k < issued
+    bool ok = true;
+    for (int n = lane;; n += kProducerLanes) {
+      const int item = blockIdx.x + n * G;
+      if (item >= p.items) break;
+      const int stage = n % S;
+      const int round = n / S;
+      if (round > 0 &&
+          !mbar_wait(smem_u32(&ctl.empty[stage]), static_cast<uint32_t>((round - 1) & 1),
+                     abort_flag, status, kDevTimeoutLoad)) {
+        ok = false;
+        break;
+      }
+      fill_stage(p, smem, item, stage, smem_u32(&ctl.full[stage]), policy);
+      ++issued;
+    }
+    (void)ok;
+    // Before leaving, wait (bounded) until this lane's fills have landed: if
+    // the consumers abort, nothing else would keep the CTA alive while copies
+    // into its shared memory are in flight. A fill superseded by a later fill
+    // of the same stage (item m + S or later) has landed already; its phase
+    // parity may have come round again, so it is skipped.
+    const int last = issued > 0 ? lane + kProducerLanes * (issued - 1) : -1;
+    const int max_last = __reduce_max_sync((1u << kProducerLanes) - 1, last);
+    for (int k = issued - 1; k >= 0; --k) {
+      const int m = lane + kProducerLanes * k;
+      if (m + S <= max_last) break;
+      mbar_wait_drain(smem_u32(&ctl.full[m % S]), static_cast<uint32_t>((m / S) & 1), status);
+    }
+    return;
   }
 
-  const float* __restrict__ w = p.weight[t];
-  const float ps = p.post_scale[t];
-  const bool rope = (p.rope_mask >> t) & 1;
-  if (w != nullptr || ps != 1.0f || rope) {
-    float rinv[kV];
-    if (w != nullptr) {
-      if (!p.per_head) {
+  // ------------------------------------------------------------------ consumers
+  const int warp = (threadIdx.x >> 5) - 1;
+  const int lane = threadIdx.x & 31;
+  const int dmask = (1 << p.vpd_log2) - 1;
+  const int nvec = p.heads << p.vpd_log2;
+  const int nvec_all = nslots << p.vpd_log2;
+  const int iters = (nvec + 31) >> 5;
+  const int seg = 1 << p.vpd_log2;  // lanes per head (8, 16 or 32)
+  const int tok_table = 32 << p.vpd_log2;
+  for (int n = warp, item = blockIdx.x + warp * G; item < p.items;
+       n += kConsumerWarps, item += kConsumerWarps * G) {
+    const int stage = n % S;
+    if (!mbar_wait(smem_u32(&ctl.full[stage]), static_cast<uint32_t>((n / S) & 1), abort_flag,
+                   status, kDevTimeoutSoftmax))
+      return;
+    int t, b, s0, count;
+    item_coords(p, item, t, b, s0, count);
+    const uint4* __restrict__ w =
+        p.weight_off[t] >= 0 ? reinterpret_cast<const uint4*>(smem + p.weight_off[t]) : nullptr;
+    const bool norm = w != nullptr;
+    const float ps = p.post_scale[t];
+    const bool rope = (p.rope_mask >> t) & 1;
+    const bool work = norm || ps != 1.0f || rope;
+    uint4* __restrict__ dst = p.dst[t] + static_cast<long long>(b) * p.item_vecs;
+    for (int r = 0; r < count; ++r) {
+      const int s = s0 + r;
+      const uint4* __restrict__ row = reinterpret_cast<const uint4*>(
+          smem + p.ring_off + stage * p.stage_bytes + r * p.row_bytes);
+      const float4* __restrict__ tab = reinterpret_cast<const float4*>(
+          smem + p.table_off + stage * p.table_bytes + r * tok_table);
+      float rrow = 0.f;
+      if (norm && !p.per_head) {
         float acc = 0.f;
-#pragma unroll
-        for (int i = 0; i < kV; ++i) {
-          float f[8];
-          unpack8(x[i], f);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) acc = fmaf(f[k], f[k], acc);
+#pragma unroll 4
+        for (int i = 0; i < iters; ++i) {
+          const int v = lane + 32 * i;
+          if (v < nvec) acc += sumsq8(row[v]);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        const float var = __fdiv_rn(acc, p.cols);
-        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-#pragma unroll
-        for (int i = 0; i < kV; ++i) rinv[i] = r;
-      } else {
-        const int seg = 1 << p.vpd_log2;  // lanes per head (8, 16 or 32)
-#pragma unroll
-        for (int i = 0; i < kV; ++i) {
-          float f[8];
-          unpack8(x[i], f);
-          float acc = 0.f;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) acc = fmaf(f[k], f[k], acc);
-          for (int o = seg >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-          const float var = __fdiv_rn(acc, p.cols);
-          rinv[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+        rrow = rms_inverse(acc, p.cols, p.eps);
+      }
+#pragma unroll 2
+      for (int i = 0; i < iters; ++i) {
+        const int v = lane + 32 * i;
+        const bool valid = v < nvec;
+        const uint4 x = valid ? row[v] : make_uint4(0, 0, 0, 0);
+        float rv = rrow;
+        if (norm && p.per_head) {
+          float a = sumsq8(x);
+          for (int o = seg >> 1; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+          rv = rms_inverse(a, p.cols, p.eps);
         }
+        if (!valid) continue;
+        const int h = v >> p.vpd_log2;
+        const int dv = v & dmask;
+        uint4 y = x;
+        if (work) {
+          const uint4 wv = norm ? w[p.per_head ? dv : v] : make_uint4(0, 0, 0, 0);
+          const float4 c = rope ? tab[dv] : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 sv = rope ? tab[seg + dv] : c;
+          y = transform8(x, norm, rv, wv, ps, rope, c, sv);
+        }
+        const HeadSlot slot = slots[h];
+        dst[slot.base + s * slot.token_stride + dv] = y;
+      }
+      // zero heads past H (head padding of the last groups)
+      for (int v = nvec + lane; v < nvec_all; v += 32) {
+        const HeadSlot slot = slots[v >> p.vpd_log2];
+        dst[slot.base + s * slot.token_stride + (v & dmask)] = make_uint4(0, 0, 0, 0);
       }
     }
-    const float* __restrict__ cs = p.cos + s * p.rope_stride;
-    const float* __restrict__ sn = p.sin + s * p.rope_stride;
-#pragma unroll
-    for (int i = 0; i < kV; ++i) {
-      const int v = i * 32 + lane;
-      if (v >= nvec) continue;
-      const int dv = v & dmask;
-      float f[8];
-      unpack8(x[i], f);
-      if (w != nullptr) {
-        const float* wp = w + (p.per_head ? 0 : (v >> p.vpd_log2) << (p.vpd_log2 + 3)) + dv * 8;
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(wp));
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(wp) + 1);
-        const float wf[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float n = round_bf16(__fmul_rn(f[k], rinv[i]));
-          f[k] = round_bf16(__fmul_rn(n, round_bf16(wf[k])));
-        }
-      }
-      if (ps != 1.0f) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) f[k] = round_bf16(__fmul_rn(f[k], ps));
-      }
-      if (rope) {
-        const float4 c = __ldg(reinterpret_cast<const float4*>(cs + dv * 4));
-        const float4 sv = __ldg(reinterpret_cast<const float4*>(sn + dv * 4));
-        const float cc[4] = {c.x, c.y, c.z, c.w};
-        const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float a = f[2 * k], bb = f[2 * k + 1];
-          f[2 * k] = __fsub_rn(__fmul_rn(a, cc[k]), __fmul_rn(bb, ss[k]));
-          f[2 * k + 1] = __fadd_rn(__fmul_rn(bb, cc[k]), __fmul_rn(a, ss[k]));
-        }
-      }
-      x[i] = pack8(f);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&ctl.empty[stage]));
   }
-
-  uint4* __restrict__ dst = p.dst[t] + b * p.item_vecs;
-#pragma unroll
-  for (int i = 0; i < kV; ++i) {
-    const int v = i * 32 + lane;
-    if (v < nvec) dst[packed_index(p, s, v >> p.vpd_log2, v & dmask)] = x[i];
-  }
-  // zero heads past H (head padding of the last groups)
-  const int nvec_all = (p.groups * p.hg) << p.vpd_log2;
-  for (int v = nvec + lane; v < nvec_all; v += 32)
-    dst[packed_index(p, s, v >> p.vpd_log2, v & dmask)] = make_uint4(0, 0, 0, 0);
 }
 
 }  // namespace prologue

@@ -685,19 +685,64 @@ extern "C" int vx_norm_rope_pack(const vx_norm_rope_pack_args* a, vx_stream_t st
   }
   const long long rows = static_cast<long long>(a->batch) * a->seq;
   if (rows == 0) return VX_OK;
-  const long long blocks = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
-  if (blocks > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "too many rows");
-  dim3 grid(static_cast<unsigned>(blocks), a->num_tensors);
+  if (static_cast<long long>(a->groups) * p.hg > kMaxHeadSlots)
+    return fail(VX_EUNSUPPORTED, "groups * ceil(heads / groups) = %d (at most %d)",
+                a->groups * p.hg, kMaxHeadSlots);
+  auto round_up = [](int x) { return (x + kStageAlign - 1) / kStageAlign * kStageAlign; };
+  p.row_bytes = static_cast<int>(row_vecs * 16);
+  const int tok_table = p.rope_mask != 0 ? a->head_dim * 4 : 0;  // cos and sin rows of a token
+  int R = std::max(1, std::min(kMaxRowsPerStage, kTargetStageBytes / p.row_bytes));
+  R = std::min(R, a->seq);
+  int off = 0;
+  for (int t = 0; t < 3; ++t) {
+    p.weight_off[t] = -1;
+    if (t < a->num_tensors && p.weight[t] != nullptr) {
+      p.weight_off[t] = off;
+      off += round_up(static_cast<int>(p.cols) * 2);
+    }
+  }
+  p.head_off = off;
+  off += round_up(a->groups * p.hg * static_cast<int>(sizeof(HeadSlot)));
+  const int fixed = off + round_up(static_cast<int>(sizeof(RingControl)));
+  // fewer rows per stage until the ring holds kMinStages stages
+  int stages = 0;
+  for (; R >= 1; --R) {
+    p.stage_bytes = round_up(R * p.row_bytes);
+    p.table_bytes = R * tok_table;
+    stages = (kSmemBudget - fixed) / (p.stage_bytes + p.table_bytes);
+    stages = std::min(kMaxStages, stages / kConsumerWarps * kConsumerWarps);
+    if (stages >= kMinStages) break;
+  }
+  if (R < 1) return fail(VX_EUNSUPPORTED, "rows too large for the shared-memory ring");
+  p.rows_per_stage = R;
+  p.blocks = (a->seq + R - 1) / R;
+  if (static_cast<long long>(p.blocks) * a->batch * a->num_tensors > 0x7fffffffLL)
+    return fail(VX_EUNSUPPORTED, "too many rows");
+  p.items = p.blocks * a->batch * a->num_tensors;
+  p.stages = stages;
+  p.ring_off = off;
+  off += stages * p.stage_bytes;
+  p.table_off = off;
+  off += stages * p.table_bytes;
+  p.ctl_off = off;
+  const size_t smem = static_cast<size_t>(off) + sizeof(RingControl);
+  p.table_mode = 0;
+  if (p.rope_mask != 0 && a->rope_sin == a->rope_cos + a->head_dim / 2 &&
+      a->rope_stride >= a->head_dim)
+    p.table_mode = a->rope_stride == a->head_dim ? 2 : 1;
+  for (int t = 0; t < a->num_tensors; ++t)
+    p.contiguous[t] = p.h_stride[t] != vpd ? 0 : (p.s_stride[t] == row_vecs ? 2 : 1);
+  int dev, sms, rc;
+  if ((rc = current_device(&dev)) != VX_OK) return rc;
+  if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
+  int* status = nullptr;
+  if ((rc = status_word(dev, &status)) != VX_OK) return rc;
+  const unsigned grid = static_cast<unsigned>(std::min<long long>(p.items, sms));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const long long per_lane = (row_vecs + 31) / 32;
-  if (per_lane <= 8)
-    norm_rope_pack_kernel<8><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
-  else if (per_lane <= 16)
-    norm_rope_pack_kernel<16><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
-  else if (per_lane <= 24)
-    norm_rope_pack_kernel<24><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
-  else
-    norm_rope_pack_kernel<32><<<grid, kWarpsPerCta * 32, 0, st>>>(p);
+  if ((rc = prepare_kernel(reinterpret_cast<const void*>(norm_rope_pack_kernel), dev,
+                           kSmemBudget)) == VX_OK)
+    norm_rope_pack_kernel<<<grid, kThreads, smem, st>>>(p, status);
+  if (rc != VX_OK) return rc;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "norm_rope_pack launch");
   return VX_OK;

@@ -71,7 +71,10 @@ def rope3d_freqs(t: int, h: int, w: int, head_dim: int, theta: float = 10000.0,
     head_dim // 2 frequency pairs split c - 2*(c//3) / c//3 / c//3 over
     T / H / W. Returns (cos, sin), each (t*h*w, head_dim // 2) float32 in
     row-major (t, h, w) token order -- the reference's (1, S, 1, D/2) arrays
-    without the broadcast axes. Built once per sequence on the host."""
+    without the broadcast axes. Built once per sequence on the host. Both are
+    views of one (S, D) [cos | sin] buffer, the layout `norm_rope_pack` reads
+    with one copy per token block; `pair_tables` gives that layout to other
+    tables."""
     if head_dim % 2:
         raise ValueError("head_dim must be even")
     c = head_dim // 2
@@ -79,17 +82,18 @@ def rope3d_freqs(t: int, h: int, w: int, head_dim: int, theta: float = 10000.0,
     if max(t, h, w) > max_seq_len:
         raise ValueError(f"grid {t}x{h}x{w} exceeds max_seq_len {max_seq_len}")
     tabs = [_axis_freqs(max_seq_len, 2 * d, theta) for d in dims]
-    out = []
+    both = np.empty((t * h * w, 2 * c), dtype=np.float32)  # [cos | sin] per token
     for k in range(2):
         ft, fh, fw = (tab[k] for tab in tabs)
-        g = np.concatenate([
+        both[:, k * c:(k + 1) * c] = np.concatenate([
             np.broadcast_to(ft[:t, None, None, :], (t, h, w, dims[0])),
             np.broadcast_to(fh[None, :h, None, :], (t, h, w, dims[1])),
             np.broadcast_to(fw[None, None, :w, :], (t, h, w, dims[2])),
         ], axis=-1).reshape(t * h * w, c)
-        g = torch.from_numpy(np.ascontiguousarray(g))
-        out.append(g.to(device) if device is not None else g)
-    return out[0], out[1]
+    tab = torch.from_numpy(both)
+    if device is not None:
+        tab = tab.to(device)
+    return tab[:, :c], tab[:, c:]
 
 
 # ------------------------------------------------------------------ launch
@@ -170,7 +174,7 @@ def norm_rope_pack(
     a.per_head = int(bool(per_head))
     a.eps = eps
     if rope is not None and rope_mask:
-        cos, sin = (t.to(device=x0.device, dtype=torch.float32).contiguous() for t in rope)
+        cos, sin = pair_tables(*rope, device=x0.device)
         if cos.shape != sin.shape or cos.shape[0] != S or cos.shape[-1] != D // 2:
             raise ValueError(f"rope tables must be ({S}, {D // 2}), got {tuple(cos.shape)}")
         keep += [cos, sin]
@@ -191,6 +195,22 @@ def norm_rope_pack(
     for t in keep:  # tables / converted weights may be freed before the kernel runs
         t.record_stream(stream)
     return out
+
+
+def pair_tables(cos: torch.Tensor, sin: torch.Tensor, device=None):
+    """(cos, sin) as float32 views of one (S, D) [cos | sin] buffer on
+    `device`: the kernel then fetches a token block's tables with one copy.
+    Tables already in that layout are returned as they are."""
+    cos = cos.to(device=device, dtype=torch.float32)
+    sin = sin.to(device=device, dtype=torch.float32)
+    half = cos.shape[-1]
+    paired = (cos.dim() == 2 and cos.shape == sin.shape and cos.stride() == (2 * half, 1)
+              and sin.stride() == cos.stride()
+              and sin.data_ptr() == cos.data_ptr() + 4 * half and cos.data_ptr() % 16 == 0)
+    if paired:
+        return cos, sin
+    both = torch.cat([cos.reshape(-1, half), sin.reshape(-1, half)], dim=1)
+    return both[:, :half], both[:, half:]
 
 
 def slice_views(buf: torch.Tensor, groups: int, seq: int, head_dim: int,
