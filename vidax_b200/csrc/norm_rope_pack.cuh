@@ -121,9 +121,6 @@ struct RingControl {
 
 __device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
-__device__ __forceinline__ float round_bf16(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
 // Two floats -> packed bf16x2 (round to nearest even), one conversion.
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -175,56 +172,93 @@ __device__ __forceinline__ float rms_inverse(float sumsq, float cols, float eps)
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 }
 
-__device__ __forceinline__ float sumsq8(const uint4& x) {
-  float f[8];
-  unpack8(x, f);
-  float acc = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) acc = fmaf(f[k], f[k], acc);
-  return acc;
-}
-
 __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
 
-// One 16-byte vector (8 features, pairs 4 dv .. 4 dv + 3): norm (r = 1/rms,
-// wv = 8 bf16 weights), post scale, rotation by the 4 (cos, sin) pairs c / sv.
-__device__ __forceinline__ uint4 transform8(const uint4& xin, bool norm, float r, const uint4 wv,
-                                            float ps, bool rope, const float4 c, const float4 sv) {
-  uint4 y = xin;
-  if (norm) {
-    float f[8];
-    unpack8(xin, f);
+// A 16-byte vector (8 bf16 = rotation pairs 4 dv .. 4 dv + 3) as packed
+// float pairs: e[0] = (x0, x2), e[1] = (x4, x6) hold the pairs' first
+// elements, o[0] = (x1, x3), o[1] = (x5, x7) their second elements -- the
+// layout f32x2 arithmetic wants for (pair k, pair k+1) at once.
+struct Split8 {
+  uint64_t e[2], o[2];
+};
+
+__device__ __forceinline__ Split8 split8(const uint4& x) {
+  Split8 r;
+  r.e[0] = f2_pack(bf16_lo(x.x), bf16_lo(x.y));
+  r.o[0] = f2_pack(bf16_hi(x.x), bf16_hi(x.y));
+  r.e[1] = f2_pack(bf16_lo(x.z), bf16_lo(x.w));
+  r.o[1] = f2_pack(bf16_hi(x.z), bf16_hi(x.w));
+  return r;
+}
+
+// Back to 8 bf16 (round to nearest even).
+__device__ __forceinline__ uint4 join8(const Split8& v) {
+  float e0, e1, e2, e3, o0, o1, o2, o3;
+  f2_unpack(v.e[0], e0, e1);
+  f2_unpack(v.o[0], o0, o1);
+  f2_unpack(v.e[1], e2, e3);
+  f2_unpack(v.o[1], o2, o3);
+  return make_uint4(pack2(e0, o0), pack2(e1, o1), pack2(e2, o2), pack2(e3, o3));
+}
+
+// sum of squares of the 8 features into a packed accumulator pair
+__device__ __forceinline__ uint64_t sumsq8_acc(const uint4& x, uint64_t acc) {
+  const Split8 v = split8(x);
+  acc = f2_fma(v.e[0], v.e[0], acc);
+  acc = f2_fma(v.o[0], v.o[0], acc);
+  acc = f2_fma(v.e[1], v.e[1], acc);
+  return f2_fma(v.o[1], v.o[1], acc);
+}
+
+__device__ __forceinline__ float f2_sum(uint64_t acc) {
+  float a, b;
+  f2_unpack(acc, a, b);
+  return a + b;
+}
+
+// n = bf16(x * r), y = bf16(n * w) (bf16 x bf16 products are exact in
+// float32: one rounding, as the reference's bf16 multiply); rr = (r, r).
+__device__ __forceinline__ uint4 norm8(const uint4& x, uint64_t rr, const uint4& wv) {
+  Split8 v = split8(x);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) f[k] = __fmul_rn(f[k], r);
-    // bf16 x bf16 products are exact in float32: one rounding, as the
-    // reference's bf16 multiply
-    y = make_uint4(mul_bf16x2(pack2(f[0], f[1]), wv.x), mul_bf16x2(pack2(f[2], f[3]), wv.y),
-                   mul_bf16x2(pack2(f[4], f[5]), wv.z), mul_bf16x2(pack2(f[6], f[7]), wv.w));
+  for (int k = 0; k < 2; ++k) {
+    v.e[k] = f2_mul(v.e[k], rr);
+    v.o[k] = f2_mul(v.o[k], rr);
   }
-  if (ps != 1.0f || rope) {
-    float f[8];
-    unpack8(y, f);
-    if (ps != 1.0f) {
+  const uint4 n = join8(v);
+  return make_uint4(mul_bf16x2(n.x, wv.x), mul_bf16x2(n.y, wv.y), mul_bf16x2(n.z, wv.z),
+                    mul_bf16x2(n.w, wv.w));
+}
+
+__device__ __forceinline__ uint4 scale8(const uint4& x, float ps) {
+  float f[8];
+  unpack8(x, f);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) f[k] = round_bf16(__fmul_rn(f[k], ps));
-    }
-    if (rope) {
-      const float cc[4] = {c.x, c.y, c.z, c.w};
-      const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
+  for (int k = 0; k < 8; ++k) f[k] = __fmul_rn(f[k], ps);
+  return pack8(f);
+}
+
+// (a, b) -> (a c - b s, b c + a s) on the 4 pairs, every product and sum
+// rounded in float32; c = (c0..c3), sn = (s0..s3) of the 4 pairs. Scalar
+// __fmul_rn / __fadd_rn / __fsub_rn: the compiler never fuses them into an
+// FMA (packed f32x2 multiplies followed by adds were contracted, changing the
+// rounding).
+__device__ __forceinline__ uint4 rope8(const uint4& x, const float4& c, const float4& sn) {
+  float f[8];
+  unpack8(x, f);
+  const float cc[4] = {c.x, c.y, c.z, c.w};
+  const float ss[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float a = f[2 * k], bb = f[2 * k + 1];
-        f[2 * k] = __fsub_rn(__fmul_rn(a, cc[k]), __fmul_rn(bb, ss[k]));
-        f[2 * k + 1] = __fadd_rn(__fmul_rn(bb, cc[k]), __fmul_rn(a, ss[k]));
-      }
-    }
-    y = pack8(f);
+  for (int k = 0; k < 4; ++k) {
+    const float a = f[2 * k], b = f[2 * k + 1];
+    f[2 * k] = __fsub_rn(__fmul_rn(a, cc[k]), __fmul_rn(b, ss[k]));
+    f[2 * k + 1] = __fadd_rn(__fmul_rn(b, cc[k]), __fmul_rn(a, ss[k]));
   }
-  return y;
+  return pack8(f);
 }
 
 // Issues the bulk copies of item `item` into stage `stage` (producer lane).
@@ -267,6 +301,75 @@ __device__ __forceinline__ void fill_stage(const NormRopeParams& p, uint8_t* sme
                     tok_table / 2, full, policy);
         }
       }
+    }
+  }
+}
+
+// One token row of one tensor: kNorm 0 none, 1 whole row, 2 per head.
+template <int kNorm, bool kScale, bool kRope>
+__device__ __forceinline__ void process_row(const NormRopeParams& p, const uint4* __restrict__ row,
+                                            const float4* __restrict__ tab,
+                                            const uint4* __restrict__ w, float ps,
+                                            uint4* __restrict__ dst, const HeadSlot* slots,
+                                            int s, int lane) {
+  const int dmask = (1 << p.vpd_log2) - 1;
+  const int nvec = p.heads << p.vpd_log2;
+  const int iters = (nvec + 31) >> 5;
+  uint64_t rr = 0;
+  if (kNorm == 1) {
+    uint64_t acc = 0;
+#pragma unroll 4
+    for (int i = 0; i < iters; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nvec) acc = sumsq8_acc(row[v], acc);
+    }
+    float tot = f2_sum(acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    const float r = rms_inverse(tot, p.cols, p.eps);
+    rr = f2_pack(r, r);
+  }
+#pragma unroll 2
+  for (int i = 0; i < iters; ++i) {
+    const int v = lane + 32 * i;
+    const bool valid = v < nvec;
+    const int dv = v & dmask;
+    uint4 y = valid ? row[v] : make_uint4(0, 0, 0, 0);
+    if (kNorm == 2) {
+      float a = f2_sum(sumsq8_acc(y, 0));
+      for (int o = (dmask + 1) >> 1; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      const float r = rms_inverse(a, p.cols, p.eps);
+      rr = f2_pack(r, r);
+    }
+    if (!valid) continue;
+    if (kNorm != 0) y = norm8(y, rr, w[kNorm == 2 ? dv : v]);
+    if (kScale) y = scale8(y, ps);
+    if (kRope) y = rope8(y, tab[dv], tab[dmask + 1 + dv]);
+    const HeadSlot slot = slots[v >> p.vpd_log2];
+    dst[slot.base + s * slot.token_stride + dv] = y;
+  }
+}
+
+template <int kNorm, bool kScale, bool kRope>
+__device__ __noinline__ void process_rows(const NormRopeParams& p, const uint8_t* smem, int stage,
+                                          int t, int b, int s0, int count, int lane) {
+  const uint4* w = kNorm != 0 ? reinterpret_cast<const uint4*>(smem + p.weight_off[t]) : nullptr;
+  const HeadSlot* slots = reinterpret_cast<const HeadSlot*>(smem + p.head_off);
+  uint4* dst = p.dst[t] + static_cast<long long>(b) * p.item_vecs;
+  const int dmask = (1 << p.vpd_log2) - 1;
+  const int nvec = p.heads << p.vpd_log2;
+  const int nvec_all = (p.groups * p.hg) << p.vpd_log2;
+  for (int r = 0; r < count; ++r) {
+    const int s = s0 + r;
+    const uint4* row = reinterpret_cast<const uint4*>(smem + p.ring_off + stage * p.stage_bytes +
+                                                      r * p.row_bytes);
+    const float4* tab = reinterpret_cast<const float4*>(
+        smem + p.table_off + stage * p.table_bytes + r * (32 << p.vpd_log2));
+    process_row<kNorm, kScale, kRope>(p, row, tab, w, p.post_scale[t], dst, slots, s, lane);
+    // zero heads past H (head padding of the last groups)
+    for (int v = nvec + lane; v < nvec_all; v += 32) {
+      const HeadSlot slot = slots[v >> p.vpd_log2];
+      dst[slot.base + s * slot.token_stride + (v & dmask)] = make_uint4(0, 0, 0, 0);
     }
   }
 }
@@ -344,12 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1) norm_rope_pack_kernel(
   // ------------------------------------------------------------------ consumers
   const int warp = (threadIdx.x >> 5) - 1;
   const int lane = threadIdx.x & 31;
-  const int dmask = (1 << p.vpd_log2) - 1;
-  const int nvec = p.heads << p.vpd_log2;
-  const int nvec_all = nslots << p.vpd_log2;
-  const int iters = (nvec + 31) >> 5;
-  const int seg = 1 << p.vpd_log2;  // lanes per head (8, 16 or 32)
-  const int tok_table = 32 << p.vpd_log2;
   for (int n = warp, item = blockIdx.x + warp * G; item < p.items;
        n += kConsumerWarps, item += kConsumerWarps * G) {
     const int stage = n % S;
@@ -358,60 +455,27 @@ __global__ void __launch_bounds__(kThreads, 1) norm_rope_pack_kernel(
       return;
     int t, b, s0, count;
     item_coords(p, item, t, b, s0, count);
-    const uint4* __restrict__ w =
-        p.weight_off[t] >= 0 ? reinterpret_cast<const uint4*>(smem + p.weight_off[t]) : nullptr;
-    const bool norm = w != nullptr;
-    const float ps = p.post_scale[t];
+    const int norm = p.weight_off[t] < 0 ? 0 : (p.per_head ? 2 : 1);
+    const bool scale = p.post_scale[t] != 1.0f;
     const bool rope = (p.rope_mask >> t) & 1;
-    const bool work = norm || ps != 1.0f || rope;
-    uint4* __restrict__ dst = p.dst[t] + static_cast<long long>(b) * p.item_vecs;
-    for (int r = 0; r < count; ++r) {
-      const int s = s0 + r;
-      const uint4* __restrict__ row = reinterpret_cast<const uint4*>(
-          smem + p.ring_off + stage * p.stage_bytes + r * p.row_bytes);
-      const float4* __restrict__ tab = reinterpret_cast<const float4*>(
-          smem + p.table_off + stage * p.table_bytes + r * tok_table);
-      float rrow = 0.f;
-      if (norm && !p.per_head) {
-        float acc = 0.f;
-#pragma unroll 4
-        for (int i = 0; i < iters; ++i) {
-          const int v = lane + 32 * i;
-          if (v < nvec) acc += sumsq8(row[v]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        rrow = rms_inverse(acc, p.cols, p.eps);
-      }
-#pragma unroll 2
-      for (int i = 0; i < iters; ++i) {
-        const int v = lane + 32 * i;
-        const bool valid = v < nvec;
-        const uint4 x = valid ? row[v] : make_uint4(0, 0, 0, 0);
-        float rv = rrow;
-        if (norm && p.per_head) {
-          float a = sumsq8(x);
-          for (int o = seg >> 1; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-          rv = rms_inverse(a, p.cols, p.eps);
-        }
-        if (!valid) continue;
-        const int h = v >> p.vpd_log2;
-        const int dv = v & dmask;
-        uint4 y = x;
-        if (work) {
-          const uint4 wv = norm ? w[p.per_head ? dv : v] : make_uint4(0, 0, 0, 0);
-          const float4 c = rope ? tab[dv] : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float4 sv = rope ? tab[seg + dv] : c;
-          y = transform8(x, norm, rv, wv, ps, rope, c, sv);
-        }
-        const HeadSlot slot = slots[h];
-        dst[slot.base + s * slot.token_stride + dv] = y;
-      }
-      // zero heads past H (head padding of the last groups)
-      for (int v = nvec + lane; v < nvec_all; v += 32) {
-        const HeadSlot slot = slots[v >> p.vpd_log2];
-        dst[slot.base + s * slot.token_stride + (v & dmask)] = make_uint4(0, 0, 0, 0);
-      }
+    const int mode = norm * 4 + (scale ? 2 : 0) + (rope ? 1 : 0);
+    switch (mode) {
+#define VX_ROWS(m, N, SC, RO) \
+  case m: process_rows<N, SC, RO>(p, smem, stage, t, b, s0, count, lane); break;
+      VX_ROWS(0, 0, false, false)
+      VX_ROWS(1, 0, false, true)
+      VX_ROWS(2, 0, true, false)
+      VX_ROWS(3, 0, true, true)
+      VX_ROWS(4, 1, false, false)
+      VX_ROWS(5, 1, false, true)
+      VX_ROWS(6, 1, true, false)
+      VX_ROWS(7, 1, true, true)
+      VX_ROWS(8, 2, false, false)
+      VX_ROWS(9, 2, false, true)
+      VX_ROWS(10, 2, true, false)
+      VX_ROWS(11, 2, true, true)
+#undef VX_ROWS
+      default: break;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&ctl.empty[stage]));
