@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 B, S_GLOBAL, H, D = 1, 75600, 40, 128
 WORKLOAD = "cfg3: Ulysses self-attention layer, Wan2.1-14B 720p/81f (B=1, S=75600, H=40, D=128, bf16)"
 FALLBACK_PEAK_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one attn_fwd_kernel launch
 # per (head x token), from the ncu capture of the (1, 32760, 8, 128) case
 # (profiles/attn_fwd_dense_h8.md: 248.6 MB / (8 x 32760)); traffic grows with
@@ -50,6 +51,15 @@ TRAFFIC_BYTES_PER_HEAD_TOKEN = 948.6
 
 def flops(b, h, sq, sk, d):
     return 4.0 * b * h * sq * sk * d
+
+
+def load_hbm_peak():
+    """Measured HBM copy bandwidth (GB/s) and its source."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return FALLBACK_HBM_GBS, "fallback"
 
 
 def load_peaks():
@@ -428,6 +438,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             tf = fl / (kms / 1e3) / 1e12
             secondary[case] = {"desc": desc, "ms": round(kms, 4), "tflops": round(tf, 2),
                                "frac_of_burst_peak": round(tf / burst_peak, 4)}
+        # the fused pre-attention step (RMSNorm + RoPE + send packing) of this
+        # layer, per rank at N = 1 and N = 8: HBM-bound
+        hbm, hbm_src = load_hbm_peak()
+        for case in (f"prologue:{S_GLOBAL},{H},1", f"prologue:{S_GLOBAL // 8},{H},8"):
+            fn, _, desc = kernel_case(case, dev)
+            kms = time_launches(fn, 20, 3)
+            gbs = kernel_case_bytes(case) / (kms / 1e3) / 1e9
+            secondary[case] = {"desc": desc, "ms": round(kms, 4), "gbs": round(gbs, 1),
+                               "frac_of_hbm": round(gbs / hbm, 4), "hbm_peak_source": hbm_src}
         assert _lib.device_status() == 0
 
     cpu = None
