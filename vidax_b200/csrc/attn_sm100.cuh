@@ -480,12 +480,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) pin32(sr[c]);
 
-        geo.mask_scores(j, sr);
+        const uint32_t active = geo.mask_scores(j, sr);
 
         // row max: 3-input max over 128 scores, 4 independent chains
         float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
+          if (!((active >> c) & 1u)) continue;  // warp-uniform: no visible key
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             mx0 = fmax3(mx0, __uint_as_float(sr[c][i + 0]), __uint_as_float(sr[c][i + 1]));
@@ -528,6 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
+          if (!((active >> c) & 1u)) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             float x0, x1, e0, e1;
@@ -554,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ls1 += e1;
             }
             pk[i] = pack_bf16x2(e0, e1);
+          }
           }
           tmem_st16(t_s + c * 16, pk);
           if ((kSplitP && c == 1) || c == 3) {
@@ -662,7 +668,9 @@ struct DenseGeo {
       tma_load_4d(dst + c * kHalfBytes, tm, bar, 64 * c, hk, j * kBlockN, b, pol);
   }
   __device__ void softmax_setup(int wg, int row) { row_global = q0 + wg * kBlockM + row; }
-  __device__ void mask_scores(int j, uint32_t (&sr)[4][32]) const {
+  // Masks keys past kv_valid; every 32-column chunk stays active (the
+  // softmax processes all four).
+  __device__ uint32_t mask_scores(int j, uint32_t (&sr)[4][32]) const {
     const int rem = kv_valid - j * kBlockN;
     if (rem < kBlockN) {
 #pragma unroll
@@ -671,6 +679,7 @@ struct DenseGeo {
         for (int i = 0; i < 32; ++i)
           if (c * 32 + i >= rem) sr[c][i] = 0xff800000u;
     }
+    return 0xfu;
   }
   __device__ __nv_bfloat16* row_ptr() const {
     return p.o + b * p.o_sb + static_cast<long long>(row_global) * p.o_ss + h * p.o_sh;
@@ -761,6 +770,7 @@ struct NaGeo {
   int u0[3], n_ax[3];     // CTA key union start and tiles per axis
   int wu0[2][3], wu1[2][3];  // per query tile key union [wu0, wu1)
   int n_tiles;
+  uint32_t div_w, div_h;  // ceil(2^32 / n_ax[2]), ceil(2^32 / n_ax[1]) (0 for n = 1)
   // softmax row state
   int qc[3];              // query coordinates of this thread's row
   int ws[3];              // window starts
@@ -815,14 +825,18 @@ struct NaGeo {
       n_ax[a] = cu1[a] > cu0[a] ? (cu1[a] - cu0[a] + kvb[a] - 1) / kvb[a] : 0;
     }
     n_tiles = n_ax[0] * n_ax[1] * n_ax[2];
+    div_w = n_ax[2] > 1 ? 0xffffffffu / static_cast<uint32_t>(n_ax[2]) + 1u : 0u;
+    div_h = n_ax[1] > 1 ? 0xffffffffu / static_cast<uint32_t>(n_ax[1]) + 1u : 0u;
   }
 
   __device__ int num_kv_tiles() const { return n_tiles; }
+  // j -> tile origin; quotients by multiply-high with ceil(2^32 / n), exact
+  // for j, n < 2^16 (tile counts here are below 2^12).
   __device__ void tile_origin(int j, int (&o)[3]) const {
-    const int jw = j % n_ax[2];
-    const int r = j / n_ax[2];
-    const int jh = r % n_ax[1];
-    const int jt = r / n_ax[1];
+    const int r = n_ax[2] > 1 ? static_cast<int>(__umulhi(static_cast<uint32_t>(j), div_w)) : j;
+    const int jw = j - r * n_ax[2];
+    const int jt = n_ax[1] > 1 ? static_cast<int>(__umulhi(static_cast<uint32_t>(r), div_h)) : r;
+    const int jh = r - jt * n_ax[1];
     o[0] = u0[0] + jt * KT;
     o[1] = u0[1] + jh * KH;
     o[2] = u0[2] + jw * KW;
@@ -873,14 +887,17 @@ struct NaGeo {
   // Column c of a key tile is key (ct, ch, cw) = (c / (KH*KW), (c / KW) % KH,
   // c % KW) of the tile box; it is visible when each coordinate lies in this
   // row's window. Masks are built per axis as bit fields, then per 32-column
-  // chunk.
-  __device__ void mask_scores(int j, uint32_t (&sr)[4][32]) const {
+  // chunk. Returns the chunks (bit c) with a visible column in any row of
+  // this warp: the softmax skips the others (no mask, no exponentials; P is
+  // zero there), which leaves their scores untouched.
+  __device__ uint32_t mask_scores(int j, uint32_t (&sr)[4][32]) const {
     int o[3];
     tile_origin(j, o);
     const uint32_t tmask = bit_range(ws[0] - o[0], ws[0] + p.kt - o[0], KT);
     const uint32_t hmask = bit_range(ws[1] - o[1], ws[1] + p.kh - o[1], KH);
     const uint32_t wmask = bit_range(ws[2] - o[2], ws[2] + p.kw - o[2], KW);
     constexpr int kRowsPerChunk = 32 / KW;  // (ct, ch) rows of the tile per chunk (>= 1)
+    uint32_t active = 0;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t m = 0;
@@ -891,13 +908,19 @@ struct NaGeo {
         const bool on = ((tmask >> ct) & 1u) && ((hmask >> ch) & 1u);
         if (on) m |= (KW == 32 ? wmask : (wmask << (rr * KW)));
       }
+      if (!row_valid) m = 0;
+      if (__any_sync(0xffffffffu, m != 0u)) {
+        active |= 1u << c;
+        if (p.round_logits) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float x = __uint_as_float(sr[c][i]);
-        if (p.round_logits) x = __bfloat162float(__float2bfloat16_rn(x));
-        sr[c][i] = ((m >> i) & 1u) ? __float_as_uint(x) : 0xff800000u;
+          for (int i = 0; i < 32; ++i)
+            sr[c][i] = __float_as_uint(__bfloat162float(__float2bfloat16_rn(__uint_as_float(sr[c][i]))));
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sr[c][i] = ((m >> i) & 1u) ? sr[c][i] : 0xff800000u;
       }
     }
+    return active;
   }
   __device__ __nv_bfloat16* row_ptr() const {
     return p.o + b * p.o_sb + qc[0] * p.o_st + qc[1] * p.o_sh + qc[2] * p.o_sw +
