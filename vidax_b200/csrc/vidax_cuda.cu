@@ -541,6 +541,11 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
   p.o_sh = a->o_stride[2];
   p.o_sw = a->o_stride[3];
   p.o_shead = a->o_stride[4];
+  p.o_vec32 = (reinterpret_cast<uintptr_t>(a->o) % 32 == 0 && a->o_stride[0] % 16 == 0 &&
+               a->o_stride[1] % 16 == 0 && a->o_stride[2] % 16 == 0 &&
+               a->o_stride[3] % 16 == 0 && a->o_stride[4] % 16 == 0)
+                  ? 1
+                  : 0;
   p.status = status;
   p.B = a->batch;
   p.T = a->T;
