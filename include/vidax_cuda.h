@@ -191,6 +191,24 @@ typedef struct vx_na3d_args {
 
 int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);
 
+/* Time-slab form of vx_na3d_fwd for sequence (T-axis) sharding: q and o hold
+ * frames [q_t0, q_t0 + T) of a T_global-frame grid, k and v frames
+ * [kv_t0, kv_t0 + T_kv) (the caller's own frames plus the halo received from
+ * the ranks that own its neighbours); windows are clamped to the global grid
+ * exactly as in the unsharded call. The key frames must cover every window of
+ * the slab's queries, else VX_EINVAL. k / v strides describe the T_kv-frame
+ * buffers. No reference counterpart as a function: vidax shards the
+ * neighborhood attention of ltx2_5/diffusion_vae.py by heads only; this is
+ * the T-slab alternative of its multi-device layouts. */
+typedef struct vx_na3d_slab {
+  int32_t T_global;
+  int32_t q_t0;
+  int32_t kv_t0;
+  int32_t T_kv;
+} vx_na3d_slab;
+
+int vx_na3d_fwd_slab(const vx_na3d_args* args, const vx_na3d_slab* slab, vx_stream_t stream);
+
 /* Host helper: start_out[i] = clamp(i - K/2, 0, length - K), K = min(kernel,
  * length), i in [0, length) -- the window-start contract of _window_start
  * (diffusion_vae.py:152-164). Returns VX_EINVAL for length/kernel < 1. */

@@ -153,3 +153,68 @@ def test_na3d_head_dim_64(shape, kernel):
     assert _status_clean()
     mx, mean = compare(out.float().cpu().numpy(), na3d(q, k, v, kernel))
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,kernel,world", [
+    ((1, 21, 10, 24, 2), (5, 9, 9), 2),
+    ((1, 21, 10, 24, 2), (5, 9, 9), 8),      # 2-3 frame slabs: halo from one neighbour
+    ((2, 13, 9, 17, 1), (11, 5, 5), 4),      # halo spans several ranks
+    ((1, 7, 6, 20, 2), (3, 7, 7), 3),
+    ((1, 4, 8, 8, 1), (5, 3, 3), 4),         # one-frame slabs, window wider than a slab
+])
+def test_na3d_time_slabs_emulated_ranks(shape, kernel, world):
+    """Each rank's slab (its frames of q, the key frames it would receive in
+    the halo exchange) through vx_na3d_fwd_slab, assembled along T, equals the
+    unsharded oracle; windows clamp to the global grid, not the slab."""
+    import vidax_b200 as vx
+    from vidax_b200.na_parallel import key_ranges, slab_bounds, split_sizes
+    B, T, H, W, NH = shape
+    q, k, v = seeded_qkv((B, T, H, W, NH, 128), 900 + T + W + world, n=3)
+    q = to_bf16(q * np.float32(128 ** -0.5))
+    qd, kd, vd = _dev(q), _dev(k), _dev(v)
+    bounds = slab_bounds(split_sizes(T, world))
+    outs = []
+    for r, (kv0, kv1) in enumerate(key_ranges(bounds, kernel[0])):
+        b0, b1 = bounds[r], bounds[r + 1]
+        outs.append(vx.neighborhood_attention_3d_slab(
+            qd[:, b0:b1].contiguous(), kd[:, kv0:kv1].contiguous(), vd[:, kv0:kv1].contiguous(),
+            kernel, t_global=T, q_t0=b0, kv_t0=kv0))
+    got = torch.cat(outs, dim=1)
+    full = vx.neighborhood_attention_3d(qd, kd, vd, kernel)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    ref = na3d(q, k, v, kernel)
+    mx, mean = compare(got.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+    mx2, _ = compare(got.float().cpu().numpy(), full.float().cpu().numpy())
+    assert mx2 <= MAX_ABS, mx2
+
+
+@pytest.mark.gpu
+def test_na3d_slab_rejects_uncovered_windows():
+    import vidax_b200 as vx
+    from vidax_b200._lib import VxInvalid
+    q, k, v = seeded_qkv((1, 8, 4, 8, 1, 128), 77, n=3)
+    qd, kd, vd = _dev(q), _dev(k), _dev(v)
+    with pytest.raises(VxInvalid):   # frames 2..5 read keys 0..7 with a 5-frame window; 1..6 given
+        vx.neighborhood_attention_3d_slab(qd[:, 2:6].contiguous(), kd[:, 1:7].contiguous(),
+                                          vd[:, 1:7].contiguous(), (5, 3, 3), t_global=8,
+                                          q_t0=2, kv_t0=1)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_na3d_time_sharded_two_gpus_nccl():
+    """Real halo exchange: 2 ranks over NCCL vs the oracle of the whole grid."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29613",
+           os.path.join(root, "tests", "dist_na_check.py")]
+    res = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert "NA SP OK" in res.stdout

@@ -19,7 +19,12 @@ from .attention import (  # noqa: F401
     local_attention,
 )
 from .hostio import attention_from_host  # noqa: F401
-from .neighborhood import na3d_flops, neighborhood_attention_3d  # noqa: F401
+from .neighborhood import (  # noqa: F401
+    na3d_flops,
+    neighborhood_attention_3d,
+    neighborhood_attention_3d_slab,
+)
+from .na_parallel import neighborhood_attention_3d_sp  # noqa: F401
 from .prologue import attend, norm_rope_pack, rms_norm_rope, rope3d_freqs  # noqa: F401
 from .ulysses import (  # noqa: F401
     axis_index,

@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "vx_device_status",
     "vx_attn_fwd",
     "vx_na3d_fwd",
+    "vx_na3d_fwd_slab",
     "vx_na3d_window_start",
     "vx_ulysses_pack",
     "vx_ulysses_unpack",

@@ -742,6 +742,10 @@ struct NaParams {
   float scale_log2;
   int round_logits;        // round q.k to bf16 before the softmax (vidax's einsum output dtype)
   int o_vec32;             // o and its strides 32-byte aligned: rows stored with 32-byte stores
+  // Time slab: q / o hold frames [q_t0, q_t0 + T) and k / v frames
+  // [kv_t0, kv_t0 + T_kv) of a T_g-frame grid; windows clamp to the global
+  // grid. The unsharded call has T_kv = T_g = T and both offsets 0.
+  int T_kv, T_g, q_t0, kv_t0;
 };
 
 __device__ __forceinline__ int na_start(int i, int L, int k) {
@@ -783,9 +787,11 @@ struct NaGeo {
     head = rest % p.NH;
     b = rest / p.NH;
     head_kv = head / (p.NH / p.NHkv);
-    lim[0] = p.T;
+    lim[0] = p.T_g;  // window clamping: the global grid
     lim[1] = p.H;
     lim[2] = p.W;
+    const int qlim[3] = {p.T, p.H, p.W};  // this call's query frames (local)
+    const int qoff[3] = {p.q_t0, 0, 0};   // local -> global query coordinates
     const int ksz[3] = {p.kt, p.kh, p.kw};
     int reg[3];
     int r = unit % p.num_regions;
@@ -805,10 +811,10 @@ struct NaGeo {
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         const int a0 = org[t][a];
-        const int a1 = min(a0 + p.qbox[a], lim[a]);
+        const int a1 = min(a0 + p.qbox[a], qlim[a]);
         if (a0 < a1) {
-          wu0[t][a] = na_start(a0, lim[a], ksz[a]);
-          wu1[t][a] = na_start(a1 - 1, lim[a], ksz[a]) + ksz[a];
+          wu0[t][a] = na_start(a0 + qoff[a], lim[a], ksz[a]);
+          wu1[t][a] = na_start(a1 - 1 + qoff[a], lim[a], ksz[a]) + ksz[a];
           if (first) {
             cu0[a] = wu0[t][a];
             cu1[a] = wu1[t][a];
@@ -867,7 +873,7 @@ struct NaGeo {
                           uint64_t pol) const {
     int o[3];
     tile_origin(j, o);
-    const int bt = b * p.T + o[0];
+    const int bt = b * p.T_kv + (o[0] - p.kv_t0);
 #pragma unroll
     for (int c = 0; c < HD / 64; ++c)
       tma_load_5d(dst + c * kHalfBytes, tm, bar, 64 * c, head_kv, o[2], o[1], bt, pol);
@@ -882,8 +888,9 @@ struct NaGeo {
     qc[2] = org[t][2] + iw;
     row_valid = qc[0] < p.T && qc[1] < p.H && qc[2] < p.W;
     const int ksz[3] = {p.kt, p.kh, p.kw};
+    const int qg[3] = {min(qc[0], p.T - 1) + p.q_t0, qc[1], qc[2]};  // global query coordinates
 #pragma unroll
-    for (int a = 0; a < 3; ++a) ws[a] = na_start(min(qc[a], lim[a] - 1), lim[a], ksz[a]);
+    for (int a = 0; a < 3; ++a) ws[a] = na_start(min(qg[a], lim[a] - 1), lim[a], ksz[a]);
   }
   // Column c of a key tile is key (ct, ch, cw) = (c / (KH*KW), (c / KW) % KH,
   // c % KW) of the tile box; it is visible when each coordinate lies in this

@@ -482,7 +482,16 @@ int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out) {
   return VX_OK;
 }
 
-int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
+static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_stream_t stream);
+
+int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) { return na3d_launch(a, nullptr, stream); }
+
+int vx_na3d_fwd_slab(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_stream_t stream) {
+  if (slab == nullptr) return fail(VX_EINVAL, "slab is NULL");
+  return na3d_launch(a, slab, stream);
+}
+
+static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_stream_t stream) {
   using namespace vx::attn;
   if (a == nullptr) return fail(VX_EINVAL, "args is NULL");
   if (a->batch < 0 || a->T < 0 || a->H < 0 || a->W < 0 || a->heads <= 0 || a->heads_kv <= 0)
@@ -502,9 +511,26 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
     if (a->o_stride[i] <= 0 || a->o_stride[i] % 8 != 0)
       return fail(VX_EINVAL, "o stride[%d] must be a positive multiple of 8 elements", i);
 
+  // time slab: query frames [q_t0, q_t0 + T), key frames [kv_t0, kv_t0 + T_kv)
+  // of a T_g-frame grid (the whole grid without a slab)
+  const int T_g = slab ? slab->T_global : a->T;
+  const int q_t0 = slab ? slab->q_t0 : 0;
+  const int kv_t0 = slab ? slab->kv_t0 : 0;
+  const int T_kv = slab ? slab->T_kv : a->T;
   const int lim[3] = {a->T, a->H, a->W};
-  const int ksz[3] = {std::min(a->kernel_t, a->T), std::min(a->kernel_h, a->H),
+  const int ksz[3] = {std::min(a->kernel_t, T_g), std::min(a->kernel_h, a->H),
                       std::min(a->kernel_w, a->W)};
+  if (slab != nullptr) {
+    if (T_g < 1 || q_t0 < 0 || q_t0 + a->T > T_g || kv_t0 < 0 || T_kv < 1 || kv_t0 + T_kv > T_g)
+      return fail(VX_EINVAL, "slab [%d, %d) / keys [%d, %d) outside a %d-frame grid", q_t0,
+                  q_t0 + a->T, kv_t0, kv_t0 + T_kv, T_g);
+    const int need0 = na_start_host(q_t0, T_g, ksz[0]);
+    const int need1 = na_start_host(q_t0 + a->T - 1, T_g, ksz[0]) + ksz[0];
+    if (kv_t0 > need0 || kv_t0 + T_kv < need1)
+      return fail(VX_EINVAL, "key frames [%d, %d) do not cover the windows [%d, %d)", kv_t0,
+                  kv_t0 + T_kv, need0, need1);
+    if ((long long)a->batch * T_kv > (1LL << 31) - 1) return fail(VX_EUNSUPPORTED, "B*T_kv too large");
+  }
   NaChoice ch;
   if (a->q_box[0] == 0 && a->q_box[1] == 0 && a->q_box[2] == 0) {
     ch = na_choose_tiling(lim, ksz);
@@ -529,9 +555,9 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
   const int HD = a->head_dim;
   if ((rc = na_tmap(&tq, "q", a->q, a->q_stride, a->batch, a->T, a->H, a->W, a->heads, HD, ch.qbox)) != VX_OK)
     return rc;
-  if ((rc = na_tmap(&tk, "k", a->k, a->k_stride, a->batch, a->T, a->H, a->W, a->heads_kv, HD, kv_box)) != VX_OK)
+  if ((rc = na_tmap(&tk, "k", a->k, a->k_stride, a->batch, T_kv, a->H, a->W, a->heads_kv, HD, kv_box)) != VX_OK)
     return rc;
-  if ((rc = na_tmap(&tv, "v", a->v, a->v_stride, a->batch, a->T, a->H, a->W, a->heads_kv, HD, kv_box)) != VX_OK)
+  if ((rc = na_tmap(&tv, "v", a->v, a->v_stride, a->batch, T_kv, a->H, a->W, a->heads_kv, HD, kv_box)) != VX_OK)
     return rc;
 
   NaParams p;
@@ -549,6 +575,10 @@ int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) {
   p.status = status;
   p.B = a->batch;
   p.T = a->T;
+  p.T_kv = T_kv;
+  p.T_g = T_g;
+  p.q_t0 = q_t0;
+  p.kv_t0 = kv_t0;
   p.H = a->H;
   p.W = a->W;
   p.NH = a->heads;

@@ -85,10 +85,39 @@ def neighborhood_attention_3d(
     softmax, as the reference's bf16 einsum does (diffusion_vae.py:222).
     `q_box` / `pair_axis` override the kernel's query tiling (tuning only).
     """
+    return _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, None)
+
+
+class Na3dSlab(ctypes.Structure):
+    _fields_ = [
+        ("T_global", ctypes.c_int32),
+        ("q_t0", ctypes.c_int32),
+        ("kv_t0", ctypes.c_int32),
+        ("T_kv", ctypes.c_int32),
+    ]
+
+
+def neighborhood_attention_3d_slab(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kernel_size: Sequence[int],
+    *, t_global: int, q_t0: int, kv_t0: int, scale: float = 1.0, round_logits: bool = False,
+) -> torch.Tensor:
+    """Neighborhood attention of one time slab: q holds frames
+    [q_t0, q_t0 + T) of a `t_global`-frame grid, k / v frames
+    [kv_t0, kv_t0 + T_kv), which must cover every window of those queries.
+    Windows clamp to the global grid, so the slab's output equals the same
+    frames of the unsharded call (`vx_na3d_fwd_slab`)."""
+    slab = Na3dSlab()
+    slab.T_global, slab.q_t0, slab.kv_t0, slab.T_kv = t_global, q_t0, kv_t0, k.shape[1]
+    return _na3d(q, k, v, kernel_size, scale, round_logits, None, 0, slab)
+
+
+def _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, slab):
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check6(name, t)
     B, T, H, W, NH, HD = q.shape
-    if k.shape[:4] != q.shape[:4] or v.shape != k.shape or k.shape[5] != HD:
+    kv_frames = k.shape[1] if slab is not None else T
+    if (k.shape[0] != B or k.shape[1] != kv_frames or k.shape[2:4] != q.shape[2:4]
+            or v.shape != k.shape or k.shape[5] != HD):
         raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} disagree")
     kt, kh, kw = (int(x) for x in kernel_size)
     q, k, v = _ready(q), _ready(k), _ready(v)
@@ -107,12 +136,18 @@ def neighborhood_attention_3d(
         a.q_box[0], a.q_box[1], a.q_box[2] = q_box
         a.pair_axis = pair_axis
     lib = _lib.load()
-    fn = lib.vx_na3d_fwd
-    fn.argtypes = [ctypes.POINTER(Na3dArgs), ctypes.c_void_p]
-    fn.restype = ctypes.c_int
     with torch.cuda.device(q.device):
         s = torch.cuda.current_stream(q.device)
-        _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)))
+        if slab is None:
+            fn = lib.vx_na3d_fwd
+            fn.argtypes = [ctypes.POINTER(Na3dArgs), ctypes.c_void_p]
+            fn.restype = ctypes.c_int
+            _lib.check(fn(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)))
+        else:
+            fn = lib.vx_na3d_fwd_slab
+            fn.argtypes = [ctypes.POINTER(Na3dArgs), ctypes.POINTER(Na3dSlab), ctypes.c_void_p]
+            fn.restype = ctypes.c_int
+            _lib.check(fn(ctypes.byref(a), ctypes.byref(slab), ctypes.c_void_p(s.cuda_stream)))
     return out
 
 
