@@ -404,11 +404,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             # public host-buffer path: transfers pipelined against the kernel
             vx.attention_from_host(hq, hk, hv, D ** -0.5, out=hout, device=dev)
             return
-        dq = hq.to(dev, non_blocking=True)
-        dk = hk.to(dev, non_blocking=True)
-        dv = hv.to(dev, non_blocking=True)
-        o = layer(dq, dk, dv)
-        hout.copy_(o, non_blocking=True)
+        # public host-buffer path: per-slice uploads land directly in the
+        # all-to-all send slabs, downloads leave from the receive slabs
+        vx.sequence_parallel_self_attention_from_host(hq, hk, hv, "sp", out=hout, device=dev)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()

@@ -32,6 +32,7 @@ from .ulysses import (  # noqa: F401
     register_axis,
     sequence_parallel_joint_self_attention,
     sequence_parallel_self_attention,
+    sequence_parallel_self_attention_from_host,
     unregister_axis,
 )
 

@@ -6,6 +6,8 @@ Mirrors the sequence-parallel half of `vidax.core.attention`:
   -- src/vidax/core/attention.py:341-388
 * `sequence_parallel_joint_self_attention(q, k, v, text_len, sp_axis_name, scale=None)`
   -- src/vidax/core/attention.py:391-464
+* `sequence_parallel_self_attention_from_host(...)`: the same layer on pinned
+  host buffers, transfers pipelined against the kernel (end-to-end form)
 
 vidax calls these inside `shard_map` with a bound mesh axis name. Here one
 process drives one GPU and the axis name is bound to a `torch.distributed`
@@ -240,6 +242,120 @@ def _ulysses_one(qb, kb, vb, ob, group, P: int, sm_scale: float, kv_valid: Optio
             unpack_heads([ro], [ob], H, sub=sub)
             ro.record_stream(side)
     comp.wait_stream(side)
+
+
+def _rows_copy(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, row_bytes: int,
+               rows: int, stream) -> None:
+    lib = _lib.load()
+    _lib.check(lib.vx_memcpy_rows_async(
+        ctypes.c_void_p(dst_ptr), dst_pitch, ctypes.c_void_p(src_ptr), src_pitch, row_bytes, rows,
+        ctypes.c_void_p(stream.cuda_stream)))
+
+
+def _slab_heads(g: int, Hg: int, off: int, hs: int, H: int):
+    """Strided heads of group g's slice [off, off + hs): first head, count valid."""
+    h0 = g * Hg + off
+    return h0, max(0, min(h0 + hs, H) - h0)
+
+
+def sequence_parallel_self_attention_from_host(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sp_axis_name: str,
+    scale: Optional[float] = None, *, out: Optional[torch.Tensor] = None,
+    device: Optional[torch.device] = None,
+) -> torch.Tensor:
+    """`sequence_parallel_self_attention` on host-resident (pinned) q, k, v
+    (B, L_local, H, D): returns the host (B, L_local, H, D) output.
+
+    The transfers double as the head-slab layout: for each pipelined slice,
+    one 2-D copy per rank group moves that group's heads of every local token
+    from host rows straight into the slice's send slab (no pack kernel), and
+    after the reverse all-to-all one 2-D copy per group moves the received
+    slab straight into the host output rows (no unpack kernel). Uploads of
+    slice j+1 and downloads of slice j-1 run on copy streams while the kernel
+    computes slice j."""
+    from .hostio import _check_host, _side_streams
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_host(name, t)
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError("self-attention needs q, k, v of equal shape")
+    group = _group(sp_axis_name)
+    P = dist.get_world_size(group)
+    B, S_loc, H, D = q.shape
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    sm_scale = D ** -0.5 if scale is None else scale
+    if out is None:
+        out = torch.empty((B, S_loc, H, D), dtype=torch.bfloat16).pin_memory()
+    Hg = -(-H // P)
+    S = P * S_loc
+    sizes = _pieces(Hg)
+    offs = [sum(sizes[:j]) for j in range(len(sizes))]
+    es = 2
+    comp = torch.cuda.current_stream(device)
+    h2d, d2h = _side_streams(device)
+    side = _side_stream(device)
+    h2d.wait_stream(comp)
+    d2h.wait_stream(comp)
+    side.wait_stream(comp)
+    keep = []
+    for b in range(B):
+        # uploads of every slice, in order, on the copy stream
+        sends, ready = [], []
+        for hs, off in zip(sizes, offs):
+            slab = [torch.empty((P, S_loc, hs, D), dtype=torch.bfloat16, device=device)
+                    for _ in range(3)]
+            for src, dst in zip((q, k, v), slab):
+                for g in range(P):
+                    h0, n = _slab_heads(g, Hg, off, hs, H)
+                    if n < hs:
+                        with torch.cuda.stream(h2d):
+                            dst[g, :, n:].zero_()  # head padding (H % P != 0)
+                    if n > 0:
+                        _rows_copy(dst[g].data_ptr(), hs * D * es,
+                                   src.data_ptr() + (b * src.stride(0) + h0 * src.stride(2)) * es,
+                                   src.stride(1) * es, n * D * es, S_loc, h2d)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            sends.append(slab)
+            ready.append(ev)
+        recvs, works = [None] * len(sizes), [None] * len(sizes)
+
+        def start_in(j):
+            # issued from the side stream so the compute stream never waits
+            # for a later slice's upload
+            recvs[j] = [torch.empty_like(t) for t in sends[j]]
+            with torch.cuda.stream(side):
+                side.wait_event(ready[j])
+                works[j] = [dist.all_to_all_single(r, t, group=group, async_op=True)
+                            for r, t in zip(recvs[j], sends[j])]
+
+        start_in(0)
+        for j, (hs, off) in enumerate(zip(sizes, offs)):
+            if j + 1 < len(sizes):
+                start_in(j + 1)
+            for w in works[j]:
+                w.wait()
+            rq, rk, rv = (t.view(1, S, hs, D) for t in recvs[j])
+            o = _timed_attention(rq, rk, rv, sm_scale, None, None)
+            ro = torch.empty((P, S_loc, hs, D), dtype=o.dtype, device=o.device)
+            w_out = dist.all_to_all_single(ro, o.view(P, S_loc, hs, D), group=group,
+                                           async_op=True)
+            with torch.cuda.stream(d2h):
+                w_out.wait()
+                for g in range(P):
+                    h0, n = _slab_heads(g, Hg, off, hs, H)
+                    if n > 0:
+                        _rows_copy(out.data_ptr() + (b * out.stride(0) + h0 * out.stride(2)) * es,
+                                   out.stride(1) * es, ro[g].data_ptr(), hs * D * es,
+                                   n * D * es, S_loc, d2h)
+            keep += [ro, o] + sends[j] + recvs[j]
+    comp.wait_stream(d2h)
+    comp.wait_stream(side)
+    for t in keep:  # device buffers stay allocated until the copies that use them ran
+        t.record_stream(h2d)
+        t.record_stream(d2h)
+        t.record_stream(side)
+    return out
 
 
 def launches_per_layer(heads: int, world: int, batch: int = 1) -> int:
