@@ -268,6 +268,70 @@ def run_kernel_only(args):
     print(json.dumps(rec), flush=True)
 
 
+def run_dit(args, rank: int, world: int, local_rank: int):
+    """One Wan2.1-1.3B DiT forward step at BASELINE config 5 (latent
+    (1, 21, 60, 104, 16) -> 32760 tokens, 512 text tokens, t = 500; random
+    weights and inputs): Ulysses sequence parallelism over the launched
+    ranks, 12 heads padded to a multiple of the rank count. Prints one JSON
+    line (whole-job matmul TFLOP/s and step time, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    import vidax_b200 as vx
+    from vidax_b200 import _lib
+    from vidax_b200.wan_dit import T2V_1_3B, init_params, step_flops, wan_dit_forward
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    cfg = T2V_1_3B
+    sp = None
+    if world > 1:
+        vx.register_axis("sp", None)
+        sp = "sp"
+    p = init_params(cfg, dev, seed=5)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    latents = torch.randn((1, 21, 60, 104, cfg.in_dim), generator=gen, device=dev).bfloat16()
+    context = torch.randn((1, cfg.text_len, cfg.text_dim), generator=gen, device=dev).bfloat16()
+    t = torch.full((1,), 500.0, device=dev)
+    rope = vx.rope3d_freqs(21, 30, 52, cfg.head_dim, device=dev)
+
+    def step():
+        return wan_dit_forward(p, cfg, latents, t, context, rope, sp_axis_name=sp)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.barrier()
+        vx.unregister_axis("sp")
+    fl = step_flops(cfg, 21 * 30 * 52)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Wan2.1-1.3B DiT forward step (cfg5), matmul TFLOP/s", "value": round(fl / (ms / 1e3) / 1e12, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16", "data": "synthetic (random weights and inputs)",
+            "config": {"workload": "cfg5: Wan2.1-1.3B t2v DiT step, latent (1, 21, 60, 104, 16), "
+                                   "32760 tokens, 30 blocks, text 512, CFG off (B=1)",
+                       "parallelism": f"ulysses-sp{world}" if world > 1 else "single",
+                       "flops_per_step": fl},
+            "out_shape": list(out.shape), "device_status": _lib.device_status()}), flush=True)
+
+
 def run_reference(args, rank: int):
     """Reference arm: vidax's CPU attention path (restated) on the host cores."""
     if rank != 0:
@@ -504,6 +568,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the extra cfg2 / cfg4 single-kernel measurements")
+    ap.add_argument("--dit", action="store_true",
+                    help="time one Wan2.1-1.3B DiT forward step (BASELINE config 5) instead")
     ap.add_argument("--kernel-only", default=None,
                     help="time one kernel case (cfg2, cfg4, attn:B,S,H, na3d:T,H,W,NH, "
                          "prologue:S,H,P) and exit")
@@ -527,7 +593,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.dit:
+            run_dit(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
