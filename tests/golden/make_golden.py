@@ -14,7 +14,8 @@ in a namespace where `jax` / `jnp` are a small numpy shim:
 * src/vidax/core/rope3d.py: `_axis_freqs`, `create_rope3d_freqs`,
   `apply_rope3d` (lines 33-111);
 * src/vidax/core/attention.py: `RMSNorm.__call__` (lines 149-162), run as a
-  plain function on a stand-in module object.
+  plain function on a stand-in module object;
+* src/vidax/core/rope3d.py: `sinusoidal_embedding_1d` (lines 15-30).
 
 The shim restates the third-party jax primitives the code calls: `jnp.take`,
 `jnp.moveaxis`, `jnp.einsum` (bf16 operands, f32 accumulation, result in the
@@ -306,6 +307,21 @@ def gen_rmsnorm():
     return out
 
 
+def gen_sinusoid():
+    """sinusoidal_embedding_1d (src/vidax/core/rope3d.py:15-30), Wan's
+    timestep embedding, at freq_dim 256 and a spread of timesteps."""
+    ns = make_namespace()
+    jnp = ns["jnp"]
+    jnp.power = np.power
+    jnp.outer = np.outer
+    jnp.cos = np.cos
+    jnp.sin = np.sin
+    load_functions("src/vidax/core/rope3d.py", ["sinusoidal_embedding_1d"], ns)
+    t = np.array([0.0, 1.0, 37.5, 500.0, 999.0], np.float32)
+    return {"sinusoid_t": t,
+            "sinusoid_emb": np.asarray(ns["sinusoidal_embedding_1d"](256, t), np.float32)}
+
+
 def main():
     if not REF or not os.path.isdir(REF):
         sys.exit("usage: make_golden.py <path-to-vidax-checkout>")
@@ -315,6 +331,7 @@ def main():
     np.savez_compressed(os.path.join(OUT_DIR, "attention_reference.npz"), **at)
     ro = gen_rope()
     ro.update(gen_rmsnorm())
+    ro.update(gen_sinusoid())
     np.savez_compressed(os.path.join(OUT_DIR, "rope_reference.npz"), **ro)
     for f in ("na3d_reference.npz", "attention_reference.npz", "rope_reference.npz"):
         print(f, os.path.getsize(os.path.join(OUT_DIR, f)), "bytes")

@@ -27,6 +27,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Dict, Optional, Tuple
 
+import numpy as np
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F
@@ -100,12 +101,16 @@ def init_params(cfg: WanConfig, device, seed: int = 0) -> Dict[str, torch.Tensor
 
 
 def sinusoidal_embedding_1d(dim: int, position: torch.Tensor) -> torch.Tensor:
-    """[cos, sin] timestep embedding in float32 (vidax/core/rope3d.py:15-30)."""
+    """[cos, sin] timestep embedding in float32 (vidax/core/rope3d.py:15-30),
+    computed on the host with numpy's float32 power / cos / sin (the math the
+    reference's formula was pinned with; B values, once per step) and placed
+    on `position`'s device."""
     half = dim // 2
-    freqs = torch.pow(torch.tensor(10000.0, device=position.device),
-                      -torch.arange(half, dtype=torch.float32, device=position.device) / half)
-    s = torch.outer(position.float(), freqs)
-    return torch.cat([torch.cos(s), torch.sin(s)], dim=1)
+    pos = position.detach().float().cpu().numpy()
+    freqs = np.power(np.float32(10000.0), -np.arange(half, dtype=np.float32) / np.float32(half))
+    s = np.outer(pos, freqs.astype(np.float32)).astype(np.float32)
+    emb = np.concatenate([np.cos(s), np.sin(s)], axis=1).astype(np.float32)
+    return torch.from_numpy(emb).to(position.device)
 
 
 def _ln(x: torch.Tensor, eps: float, w=None, b=None) -> torch.Tensor:
