@@ -66,7 +66,9 @@ def attention_from_host(
     """softmax(scale * q k^T) v for host (B, S, H, D) bf16 tensors (pinned for
     overlap), computed on `device` (default: the current CUDA device) with
     transfers pipelined against the kernel by head groups. Returns a host
-    tensor (`out` if given, else a new pinned tensor)."""
+    tensor (`out` if given, else a new pinned tensor) whose contents are
+    complete once the current CUDA stream has been synchronised (the call
+    only enqueues, like a device kernel)."""
     from .attention import flash_attention
 
     for name, t in (("q", q), ("k", k), ("v", v)):

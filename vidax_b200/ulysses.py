@@ -264,7 +264,8 @@ def sequence_parallel_self_attention_from_host(
     device: Optional[torch.device] = None,
 ) -> torch.Tensor:
     """`sequence_parallel_self_attention` on host-resident (pinned) q, k, v
-    (B, L_local, H, D): returns the host (B, L_local, H, D) output.
+    (B, L_local, H, D): returns the host (B, L_local, H, D) output, complete
+    once the current CUDA stream has been synchronised (the call enqueues).
 
     The transfers double as the head-slab layout: for each pipelined slice,
     one 2-D copy per rank group moves that group's heads of every local token
