@@ -224,6 +224,28 @@ int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out);
 int vx_memcpy_rows_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
                          int64_t row_bytes, int64_t rows, vx_stream_t stream);
 
+/* ----------------------------------------------------------------------
+ * Fused elementwise glue of the DiT block (no counterpart in vidax's FFI
+ * surface: these replace chains of framework ops around the sub-layers of
+ * WanDiTBlock, src/vidax/models/wan/wan2_1/dit.py:100-156).
+ *
+ * vx_ln_modulate: y = bf16(((x - mean) * rsqrt(var + eps) [* w + b])
+ *                          * (1 + scale[batch]) + shift[batch])
+ * per row of x (rows, dim) float32, statistics as flax's LayerNorm
+ * (var = E[x^2] - E[x]^2); w / b (dim) and scale / shift (rows /
+ * rows_per_batch, dim) are optional (NULL; scale and shift together). dim a
+ * multiple of 4, pointers 16-byte aligned.
+ *
+ * vx_gated_residual: x += float(y) * gate[batch] (gate NULL: x += y), x
+ * float32 and y bf16 of (rows, dim), gate (rows / rows_per_batch, dim); dim
+ * a multiple of 8, pointers 32-byte (x) / 16-byte (y, gate) aligned.
+ */
+int vx_ln_modulate(const float* x, void* y, const float* w, const float* b, const float* scale,
+                   const float* shift, int64_t rows, int32_t dim, int32_t rows_per_batch,
+                   float eps, vx_stream_t stream);
+int vx_gated_residual(float* x, const void* y, const float* gate, int64_t rows, int32_t dim,
+                      int32_t rows_per_batch, vx_stream_t stream);
+
 /* Self-test of the bounded-wait machinery (failure detection without a GPU
  * fault): runs one CTA that waits on an mbarrier nothing arrives on, through
  * the same bounded wait the kernels use, with a limit of `limit_cycles` SM

@@ -5,8 +5,8 @@ points where vidax casts to the compute dtype (src/vidax/models/wan/wan2_1/
 dit.py): the modulated LayerNorm outputs (:108, :131), every Dense output
 (bf16 kernels), RMSNorm (src/vidax/core/attention.py:149-162), RoPE
 (src/vidax/core/rope3d.py:89-111) and the attention outputs; the residual
-stream, modulation, timestep MLP and head LayerNorm stay float32 (:100-156,
-:296-300; dit_layers.py:205-213). Attention is `sdpa` (fp32 softmax).
+stream, modulation, timestep MLP and the head stay float32 (:100-156,
+:296-300; dit_layers.py:205-217), the output is cast to bf16. Attention is `sdpa` (fp32 softmax).
 
 Parity unpinned at the block level: flax is absent here, so the
 reference's WanDiT cannot run; the structure follows its source line by
@@ -97,7 +97,7 @@ def wan_dit_forward(params, cfg, latents, t, context, cos, sin):
                      p[b + "ffn_2_w"], p[b + "ffn_2_b"])
         x = x + hdn * g_m
     mod = p["head_modulation"] + e[:, None, :]
-    y = to_bf16(_ln(x, cfg.eps) * (1 + mod[:, 1:2]) + mod[:, 0:1])
-    y = _dense(y, p["head_w"], p["head_b"])
+    y = _ln(x, cfg.eps) * (1 + mod[:, 1:2]) + mod[:, 0:1]   # float32 head (dit_layers.py:212-217)
+    y = to_bf16(y @ p["head_w"].T + p["head_b"])
     y = y.reshape(B, grid[1], grid[2], grid[3], pt, ph, pw, cfg.out_dim).transpose(0, 1, 4, 2, 5, 3, 6, 7)
     return y.reshape(B, grid[1] * pt, grid[2] * ph, grid[3] * pw, cfg.out_dim)

@@ -65,3 +65,38 @@ def test_wan_dit_two_gpus_nccl():
     res = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "WAN SP OK" in res.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dim,affine,mod", [(256, False, True), (1536, True, False), (5120, False, True)])
+def test_ln_modulate_kernel(dim, affine, mod):
+    """vx_ln_modulate against the float32 torch composition it replaces."""
+    import torch.nn.functional as F
+    from vidax_b200.wan_dit import ln_modulate
+    g = torch.Generator(device="cuda").manual_seed(dim)
+    x = torch.randn((2, 37, dim), generator=g, device="cuda") * 3 + 0.5
+    w = torch.randn(dim, generator=g, device="cuda") if affine else None
+    b = torch.randn(dim, generator=g, device="cuda") if affine else None
+    sc = torch.randn((2, 1, dim), generator=g, device="cuda") if mod else None
+    sh = torch.randn((2, 1, dim), generator=g, device="cuda") if mod else None
+    got = ln_modulate(x, 1e-6, w, b, sc, sh).float()
+    ref = F.layer_norm(x, (dim,), w, b, 1e-6)
+    if mod:
+        ref = ref * (1 + sc) + sh
+    ref = ref.bfloat16().float()
+    diff = (got - ref).abs()
+    assert float(diff.max()) <= 2 ** -7 * float(ref.abs().max())  # one bf16 ulp of the scale
+    assert float((diff > 0).float().mean()) <= 0.02
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("gated", [True, False])
+def test_gated_residual_kernel(gated):
+    from vidax_b200.wan_dit import gated_residual_
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn((2, 45, 1536), generator=g, device="cuda")
+    y = torch.randn((2, 45, 1536), generator=g, device="cuda").bfloat16()
+    gate = torch.randn((2, 1, 1536), generator=g, device="cuda") if gated else None
+    ref = x + (y.float() * gate if gated else y.float())
+    gated_residual_(x, y, gate)
+    assert torch.allclose(x, ref, rtol=1e-6, atol=1e-6)

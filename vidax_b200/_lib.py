@@ -33,6 +33,8 @@ EXPORTED_SYMBOLS = (
     "vx_ulysses_pack",
     "vx_ulysses_unpack",
     "vx_norm_rope_pack",
+    "vx_ln_modulate",
+    "vx_gated_residual",
     "vx_memcpy_rows_async",
     "vx_selftest_wait_timeout",
 )

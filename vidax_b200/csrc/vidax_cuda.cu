@@ -19,6 +19,7 @@
 #include <utility>
 
 #include "attn_sm100.cuh"
+#include "dit_glue.cuh"
 #include "norm_rope_pack.cuh"
 #include "ulysses_pack.cuh"
 
@@ -782,6 +783,55 @@ extern "C" int vx_norm_rope_pack(const vx_norm_rope_pack_args* a, vx_stream_t st
   if (rc != VX_OK) return rc;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "norm_rope_pack launch");
+  return VX_OK;
+}
+
+extern "C" int vx_ln_modulate(const float* x, void* y, const float* w, const float* b,
+                              const float* scale, const float* shift, int64_t rows, int32_t dim,
+                              int32_t rows_per_batch, float eps, vx_stream_t stream) {
+  using namespace vx::glue;
+  if (rows < 0 || dim <= 0 || dim % 4 != 0 || rows_per_batch <= 0 ||
+      rows % rows_per_batch != 0 || !(eps >= 0.f))
+    return fail(VX_EINVAL, "bad sizes (rows %lld, dim %d, rows_per_batch %d)", (long long)rows,
+                dim, rows_per_batch);
+  if (rows == 0) return VX_OK;
+  if (x == nullptr || y == nullptr) return fail(VX_EINVAL, "x / y is NULL");
+  if ((w == nullptr) != (b == nullptr) || (scale == nullptr) != (shift == nullptr))
+    return fail(VX_EINVAL, "w and b, scale and shift come in pairs");
+  const void* ptrs[6] = {x, y, w, b, scale, shift};
+  for (const void* q : ptrs)
+    if (q != nullptr && !aligned16(q)) return fail(VX_EINVAL, "pointers must be 16-byte aligned");
+  LnParams p{x, static_cast<__nv_bfloat16*>(y), w, b, scale, shift, rows, dim, rows_per_batch, eps};
+  const long long blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "too many rows");
+  ln_modulate_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "ln_modulate launch");
+  return VX_OK;
+}
+
+extern "C" int vx_gated_residual(float* x, const void* y, const float* gate, int64_t rows,
+                                 int32_t dim, int32_t rows_per_batch, vx_stream_t stream) {
+  using namespace vx::glue;
+  if (rows < 0 || dim <= 0 || dim % 8 != 0 || rows_per_batch <= 0 || rows % rows_per_batch != 0)
+    return fail(VX_EINVAL, "bad sizes (rows %lld, dim %d, rows_per_batch %d)", (long long)rows,
+                dim, rows_per_batch);
+  if (rows == 0) return VX_OK;
+  if (x == nullptr || y == nullptr) return fail(VX_EINVAL, "x / y is NULL");
+  if (reinterpret_cast<uintptr_t>(x) % 32 != 0 || !aligned16(y) ||
+      (gate != nullptr && !aligned16(gate)))
+    return fail(VX_EINVAL, "x must be 32-byte, y and gate 16-byte aligned");
+  int dev, sms, rc;
+  if ((rc = current_device(&dev)) != VX_OK) return rc;
+  if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
+  ResidualParams p{x, static_cast<const __nv_bfloat16*>(y), gate, rows, dim, rows_per_batch};
+  const long long work = rows * (dim / 8);
+  const long long blocks = std::min<long long>((work + 255) / 256, 8LL * sms);
+  gated_residual_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                          reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gated_residual launch");
   return VX_OK;
 }
 

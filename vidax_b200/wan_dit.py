@@ -16,14 +16,17 @@ dit.py) so one step of the model runs end to end on this library:
 * `post_process` (dit.py:341-362): AdaLN head (dit_layers.py:195-217), the
   sequence all_gather of every rank's tokens, unpatchify.
 
-The projections and FFN are plain bf16 GEMMs (cuBLAS through torch); the
-attention, the pre-attention step and the Ulysses layout are this library's
-kernels. Weights are random (no checkpoints here), drawn N(0, 0.02) unless
+The projections and FFN are plain bf16 GEMMs (cuBLAS through torch, the
+FFN's bias + tanh-GELU in the cuBLASLt epilogue); the attention, the
+pre-attention step, the Ulysses layout and the block's elementwise glue
+(LayerNorm + modulation + cast, gated residual adds: one pass each) are this
+library's kernels. Weights are random (no checkpoints here), drawn N(0, 0.02) unless
 the reference initialises otherwise (modulation tables N(0, dim^-0.5),
 norm3's affine and the RMSNorm scales ones / zeros).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Dict, Optional, Tuple
 
@@ -32,6 +35,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from . import _lib
 from .attention import local_attention
 from .prologue import attend, rms_norm_rope, rope3d_freqs
 
@@ -118,6 +122,52 @@ def _ln(x: torch.Tensor, eps: float, w=None, b=None) -> torch.Tensor:
     return F.layer_norm(x.float(), (x.shape[-1],), w, b, eps)
 
 
+def ln_modulate(x: torch.Tensor, eps: float, w=None, b=None, scale=None, shift=None) -> torch.Tensor:
+    """bf16((LayerNorm(x) [* w + b]) * (1 + scale) + shift) in one pass
+    (`vx_ln_modulate`): x (B, L, dim) float32, scale / shift (B, 1, dim) or
+    (B, dim) float32."""
+    B, L, d = x.shape
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    y = torch.empty((B, L, d), dtype=torch.bfloat16, device=x.device)
+    sc = scale.reshape(B, d).contiguous() if scale is not None else None
+    sh = shift.reshape(B, d).contiguous() if shift is not None else None
+    lib = _lib.load()
+    _lib.check(lib.vx_ln_modulate(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+        ctypes.c_void_p(w.data_ptr() if w is not None else None),
+        ctypes.c_void_p(b.data_ptr() if b is not None else None),
+        ctypes.c_void_p(sc.data_ptr() if sc is not None else None),
+        ctypes.c_void_p(sh.data_ptr() if sh is not None else None),
+        ctypes.c_int64(B * L), ctypes.c_int32(d), ctypes.c_int32(L), ctypes.c_float(eps),
+        ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)))
+    return y
+
+
+def gated_residual_(x: torch.Tensor, y: torch.Tensor, gate=None) -> torch.Tensor:
+    """x += float(y) * gate in place, one pass (`vx_gated_residual`): x
+    (B, L, dim) float32, y (B, L, dim) bf16, gate (B, 1, dim) / (B, dim) or None."""
+    B, L, d = x.shape
+    if not (x.is_contiguous() and y.is_contiguous()) or y.dtype != torch.bfloat16:
+        raise ValueError("x (float32) and y (bf16) must be contiguous")
+    g = gate.reshape(B, d).contiguous() if gate is not None else None
+    lib = _lib.load()
+    _lib.check(lib.vx_gated_residual(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+        ctypes.c_void_p(g.data_ptr() if g is not None else None),
+        ctypes.c_int64(B * L), ctypes.c_int32(d), ctypes.c_int32(L),
+        ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)))
+    return x
+
+
+def _linear_gelu(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """tanh-GELU(x @ w^T + b) with bias and activation in the cuBLASLt GEMM
+    epilogue."""
+    shape = x.shape
+    h = torch._addmm_activation(b, x.reshape(-1, shape[-1]), w.t(), use_gelu=True)
+    return h.reshape(*shape[:-1], w.shape[0])
+
+
 def _gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return F.gelu(x, approximate="tanh")
 
@@ -177,28 +227,28 @@ def block_forward(p, i: int, cfg: WanConfig, x, context, t_mod, rope,
     B, L, d = x.shape
     H = cfg.num_heads
     e = p[b + "modulation"] + t_mod.float()
-    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (e[:, j:j + 1] for j in range(6))
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (e[:, j] for j in range(6))
 
-    nx = (_ln(x, cfg.eps) * (1 + scale_msa) + shift_msa).to(torch.bfloat16)
+    nx = ln_modulate(x, cfg.eps, scale=scale_msa, shift=shift_msa)
     q, k, v = (F.linear(nx, p[b + f"self_attn_{n}_w"], p[b + f"self_attn_{n}_b"]) for n in "qkv")
     o = attend(q, k, v, H, norm_q=p[b + "self_attn_norm_q"], norm_k=p[b + "self_attn_norm_k"],
                rope=rope, eps=cfg.eps, sp_axis_name=sp_axis_name)
-    o = F.linear(o, p[b + "self_attn_o_w"], p[b + "self_attn_o_b"])
-    x = x + o.float() * gate_msa
+    gated_residual_(x, F.linear(o, p[b + "self_attn_o_w"], p[b + "self_attn_o_b"]), gate_msa)
 
-    nc = _ln(x, cfg.eps, p[b + "norm3_w"], p[b + "norm3_b"]).to(torch.bfloat16)
+    nc = ln_modulate(x, cfg.eps, w=p[b + "norm3_w"], b=p[b + "norm3_b"])
     q = F.linear(nc, p[b + "cross_attn_q_w"], p[b + "cross_attn_q_b"])
     k = F.linear(context, p[b + "cross_attn_k_w"], p[b + "cross_attn_k_b"])
     v = F.linear(context, p[b + "cross_attn_v_w"], p[b + "cross_attn_v_b"])
     qn = rms_norm_rope(q, p[b + "cross_attn_norm_q"], None, H, eps=cfg.eps)
     kn = rms_norm_rope(k, p[b + "cross_attn_norm_k"], None, H, eps=cfg.eps)
     o = local_attention(qn, kn, v.view(B, -1, H, cfg.head_dim))
-    x = x + F.linear(o.reshape(B, L, d), p[b + "cross_attn_o_w"], p[b + "cross_attn_o_b"]).float()
+    gated_residual_(x, F.linear(o.reshape(B, L, d), p[b + "cross_attn_o_w"],
+                                p[b + "cross_attn_o_b"]))
 
-    nh = (_ln(x, cfg.eps) * (1 + scale_mlp) + shift_mlp).to(torch.bfloat16)
-    h = F.linear(_gelu_tanh(F.linear(nh, p[b + "ffn_0_w"], p[b + "ffn_0_b"])),
+    nh = ln_modulate(x, cfg.eps, scale=scale_mlp, shift=shift_mlp)
+    h = F.linear(_linear_gelu(nh, p[b + "ffn_0_w"], p[b + "ffn_0_b"]),
                  p[b + "ffn_2_w"], p[b + "ffn_2_b"])
-    return x + h.float() * gate_mlp
+    return gated_residual_(x, h, gate_mlp)
 
 
 def post_process(p, cfg: WanConfig, x, e, grid, sp_axis_name: Optional[str] = None):
@@ -206,8 +256,9 @@ def post_process(p, cfg: WanConfig, x, e, grid, sp_axis_name: Optional[str] = No
     token chunks in rank order (dit.py:350-354), unpatchify."""
     mod = p["head_modulation"] + e.float()[:, None, :]
     shift, scale = mod[:, 0:1], mod[:, 1:2]
-    y = (_ln(x, cfg.eps) * (1 + scale) + shift).to(torch.bfloat16)
-    y = F.linear(y, p["head_w"], p["head_b"])
+    # the head runs in float32 (its input keeps e's dtype, dit_layers.py:212-217)
+    y = _ln(x, cfg.eps) * (1 + scale) + shift
+    y = F.linear(y, p["head_w"].float(), p["head_b"].float()).to(torch.bfloat16)
     if sp_axis_name is not None:
         from .ulysses import _group
         group = _group(sp_axis_name)
