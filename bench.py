@@ -187,6 +187,7 @@ def kernel_case(name: str, dev):
     cfg2          BASELINE config 2: (1, 32760, 40, 128), per-head factors U[0.5, 2]
     cfg4          BASELINE config 4: NA over (1, 21, 30, 52, 24, 128), window 5x9x9
     na3d:T,H,W,NH window 5x9x9
+    na3d64:T,H,W,NH,kt,kh,kw  head_dim-64 neighborhood attention (LTX-2.5 decoder stages)
     prologue:S,H,P  fused RMSNorm(dim) + RoPE + Ulysses send packing of q, k, v
                   (S tokens, H heads, D=128, P destination ranks); its work is
                   algorithmic HBM bytes, not FLOPs (see kernel_case_bytes)
@@ -224,6 +225,15 @@ def kernel_case(name: str, dev):
         fl = vx.na3d_flops(1, t, hh, w, nh, D, (5, 9, 9))
         return (lambda: vx.neighborhood_attention_3d(q, k, v, (5, 9, 9))), fl, \
             f"neighborhood attention (1, {t}, {hh}, {w}, {nh}, {D}), window 5x9x9"
+    if name.startswith("na3d64:"):
+        # head_dim 64 (LTX-2.5 decoder): na3d64:T,H,W,NH,kt,kh,kw
+        t, hh, w, nh, kt, kh, kw = (int(x) for x in name.split(":")[1].split(","))
+        shape = (1, t, hh, w, nh, 64)
+        q = (rnd(shape).float() * 64 ** -0.5).bfloat16()
+        k, v = rnd(shape), rnd(shape)
+        fl = vx.na3d_flops(1, t, hh, w, nh, 64, (kt, kh, kw))
+        return (lambda: vx.neighborhood_attention_3d(q, k, v, (kt, kh, kw))), fl, \
+            f"neighborhood attention (1, {t}, {hh}, {w}, {nh}, 64), window {kt}x{kh}x{kw}"
     if name.startswith("prologue:"):
         from vidax_b200.prologue import norm_rope_pack
         from vidax_b200.ulysses import _pieces
