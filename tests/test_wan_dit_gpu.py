@@ -17,11 +17,11 @@ def _tiny(head_dim):
                      out_dim=4, freq_dim=32, text_dim=64, text_len=16)
 
 
-def _inputs(cfg, seed):
+def _inputs(cfg, seed, batch=1):
     rng = np.random.Generator(np.random.PCG64(seed))
-    latents = to_bf16(rng.standard_normal((1, 2, 8, 16, cfg.in_dim)).astype(np.float32))
-    context = to_bf16(rng.standard_normal((1, 10, cfg.text_dim)).astype(np.float32))
-    t = np.array([500.0], np.float32)
+    latents = to_bf16(rng.standard_normal((batch, 2, 8, 16, cfg.in_dim)).astype(np.float32))
+    context = to_bf16(rng.standard_normal((batch, 10, cfg.text_dim)).astype(np.float32))
+    t = np.array([500.0, 37.0][:batch], np.float32)
     return latents, context, t
 
 
@@ -30,15 +30,16 @@ def _rel(a, b):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("head_dim", [128, 64])
-def test_wan_dit_forward_matches_oracle(head_dim):
+@pytest.mark.parametrize("head_dim,batch", [(128, 1), (64, 1), (128, 2)])
+def test_wan_dit_forward_matches_oracle(head_dim, batch):
+    """batch 2 = the classifier-free-guidance batch (two timesteps here)."""
     from oracle.wan_dit_ref import wan_dit_forward as ref_forward
     from vidax_b200 import _lib
     from vidax_b200.wan_dit import init_params, wan_dit_forward
     from vidax_b200.prologue import rope3d_freqs
     cfg = _tiny(head_dim)
     p = init_params(cfg, "cuda", seed=3)
-    latents, context, t = _inputs(cfg, 5)
+    latents, context, t = _inputs(cfg, 5, batch)
     cos, sin = rope3d_freqs(2, 4, 8, cfg.head_dim)
     out = wan_dit_forward(p, cfg, torch.from_numpy(latents).cuda(), torch.from_numpy(t).cuda(),
                           torch.from_numpy(context).cuda())
@@ -46,7 +47,7 @@ def test_wan_dit_forward_matches_oracle(head_dim):
     assert _lib.device_status() == 0
     ref = ref_forward(p, cfg, latents, t, context, cos.numpy(), sin.numpy())
     got = out.float().cpu().numpy()
-    assert got.shape == ref.shape == (1, 2, 8, 16, cfg.out_dim)
+    assert got.shape == ref.shape == (batch, 2, 8, 16, cfg.out_dim)
     assert _rel(got, ref) <= 2e-2, _rel(got, ref)
 
 
