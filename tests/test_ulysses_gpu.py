@@ -109,3 +109,16 @@ def test_sub_group_pack_unpack_bit_exact(H, P, hs):
         assert torch.equal(packed, ref)
         unpack_heads([packed], [back], H, sub=sub)
     assert torch.equal(back, x)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ulysses_qsplit_two_gpus_nccl():
+    """Query-split heads (3, 5, 7 heads on 2 ranks) over NCCL vs the oracle."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29617",
+           os.path.join(ROOT, "tests", "dist_qsplit_check.py")]
+    res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert "QSPLIT OK" in res.stdout

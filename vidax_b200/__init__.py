@@ -25,6 +25,7 @@ from .neighborhood import (  # noqa: F401
     neighborhood_attention_3d_slab,
 )
 from .na_parallel import neighborhood_attention_3d_sp  # noqa: F401
+from .ulysses_qsplit import sequence_parallel_self_attention_qsplit  # noqa: F401
 from .prologue import attend, norm_rope_pack, rms_norm_rope, rope3d_freqs  # noqa: F401
 from .ulysses import (  # noqa: F401
     axis_index,
