@@ -6,7 +6,6 @@ import datetime
 import os
 import sys
 
-import numpy as np
 import torch
 import torch.distributed as dist
 

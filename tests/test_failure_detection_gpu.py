@@ -1,7 +1,6 @@
 """Failure detection without a GPU fault: a bounded device-side wait that can
 never complete gives up, records its code in the device status word, and the
 context stays usable for the next kernel."""
-import numpy as np
 import pytest
 import torch
 
