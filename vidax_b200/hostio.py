@@ -80,11 +80,15 @@ def attention_from_host(
     group = H // Hkv
     if device is None:
         device = torch.device("cuda", torch.cuda.current_device())
+    # groups cover whole KV heads; the first and the last are small, since
+    # only the first group's upload and the last group's download are not
+    # hidden behind a kernel
     if heads_per_group is None:
-        heads_per_group = max(1, min(H, 8))
-    # groups cover whole KV heads
-    kv_per_group = max(1, heads_per_group // group)
-    hq_per_group = kv_per_group * group
+        kv_per_group = max(1, min(Hkv, 8 // group if group < 8 else 1))
+        edge = max(1, Hkv // 20)
+    else:
+        kv_per_group = max(1, heads_per_group // group)
+        edge = kv_per_group
     if out is None:
         out = torch.empty((B, Sq, H, D), dtype=torch.bfloat16).pin_memory()
     qd = torch.empty((B, Sq, H, D), dtype=torch.bfloat16, device=device)
@@ -97,7 +101,14 @@ def attention_from_host(
     h2d, d2h = _side_streams(device)
     h2d.wait_stream(comp)   # device buffers may reuse memory the compute stream just freed
     d2h.wait_stream(comp)
-    groups = [(g0, min(Hkv, g0 + kv_per_group)) for g0 in range(0, Hkv, kv_per_group)]
+    sizes = [min(edge, Hkv)]
+    while sum(sizes) < Hkv:
+        left = Hkv - sum(sizes)
+        sizes.append(left if left <= edge else min(kv_per_group, left - edge))
+    groups = []
+    for n in sizes:
+        g0 = groups[-1][1] if groups else 0
+        groups.append((g0, g0 + n))
     ready = []
     for k0, k1 in groups:
         q0, q1 = k0 * group, k1 * group
