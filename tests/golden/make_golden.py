@@ -8,9 +8,10 @@ in a namespace where `jax` / `jnp` are a small numpy shim:
 * src/vidax/models/ltx2_5/diffusion_vae.py: `_window_start`, `_gather_window`,
   `neighborhood_attention_3d` (lines 152-234);
 * src/vidax/core/attention.py: `chunk_by_rank`, `local_attention`,
-  `dot_product_attention`, `sequence_parallel_self_attention` (lines
-  132-146, 321-388, 467-533), run on P threads (one per emulated device)
-  whose `jax.lax.all_to_all` / `axis_index` meet at a barrier;
+  `dot_product_attention`, `sequence_parallel_self_attention`,
+  `sequence_parallel_joint_self_attention` (lines 132-146, 321-533), run on
+  P threads (one per emulated device) whose `jax.lax.all_to_all` /
+  `all_gather` / `axis_index` meet at a barrier;
 * src/vidax/core/rope3d.py: `_axis_freqs`, `create_rope3d_freqs`,
   `apply_rope3d` (lines 33-111);
 * src/vidax/core/attention.py: `RMSNorm.__call__` (lines 149-162), run as a
@@ -119,6 +120,15 @@ class _Collective:
         self.barrier.wait()
         return res
 
+    def all_gather(self, x, axis_name, axis, tiled=False):
+        assert tiled
+        r = self.local.rank
+        self.slots[r] = np.asarray(x)
+        self.barrier.wait()
+        res = np.concatenate([self.slots[src] for src in range(self.P)], axis=axis)
+        self.barrier.wait()
+        return res
+
     def dynamic_slice_in_dim(self, x, start, size, axis=0):
         return np.take(x, np.arange(int(start), int(start) + size), axis=axis)
 
@@ -133,6 +143,7 @@ def make_namespace(coll=None):
     lax = types.SimpleNamespace(scan=_scan)
     if coll is not None:
         lax.all_to_all = coll.all_to_all
+        lax.all_gather = coll.all_gather
         lax.axis_index = coll.axis_index
         lax.dynamic_slice_in_dim = coll.dynamic_slice_in_dim
     else:
@@ -238,6 +249,30 @@ def gen_attention():
             t.join()
         out[f"sp{P}_q"], out[f"sp{P}_k"], out[f"sp{P}_v"] = (x.astype(np.float32) for x in (qg, kg, vg))
         out[f"sp{P}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
+    # joint [text; visual] Ulysses (CogVideoX layout): text replicated, visual chunked
+    for P, (B, T, S, H, D) in ((2, (1, 5, 16, 4, 8)), (4, (2, 7, 24, 8, 8))):
+        coll = _Collective(P)
+        ns_p = load_functions("src/vidax/core/attention.py",
+                              names + ["sequence_parallel_joint_self_attention"],
+                              make_namespace(coll))
+        qg, kg, vg = (seeded((B, T + S, H, D), 110 + P + i) for i in range(3))
+        results = [None] * P
+        S_loc = S // P
+
+        def worker(r):
+            coll.local.rank = r
+            loc = [np.concatenate([x[:, :T], x[:, T + r * S_loc:T + (r + 1) * S_loc]], axis=1)
+                   for x in (qg, kg, vg)]
+            results[r] = ns_p["sequence_parallel_joint_self_attention"](*loc, T, "sp")
+
+        threads = [threading.Thread(target=worker, args=(r,)) for r in range(P)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        out[f"joint{P}_q"], out[f"joint{P}_k"], out[f"joint{P}_v"] = (x.astype(np.float32) for x in (qg, kg, vg))
+        out[f"joint{P}_text_len"] = np.array([T], np.int32)
+        out[f"joint{P}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
     return out
 
 

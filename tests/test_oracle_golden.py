@@ -137,3 +137,19 @@ def test_patchify_round_trip_and_oracle_order():
     # patch vector = (pt, ph, pw, C) of one patch
     assert torch.equal(p[1, 3 * 5 + 2 * 5 + 4].reshape(2, 2, 2, 3), x[1, 2:4, 4:6, 8:10])
     assert torch.equal(unpatchify(p, (2, 2, 3, 5), (2, 2, 2), 3), x)
+
+
+@pytest.mark.parametrize("P", [2, 4])
+def test_joint_ulysses_matches_reference_code(attn_gold, P):
+    """The reference's joint [text; visual] Ulysses per emulated rank: the
+    text rows (all-gathered over heads, identical on every rank) and the
+    rank's visual chunk equal attention over the global joint sequence."""
+    qg, kg, vg = (attn_gold[f"joint{P}_{n}"] for n in "qkv")
+    T = int(attn_gold[f"joint{P}_text_len"][0])
+    ref = attn_gold[f"joint{P}_o"]                        # (P, B, T + S/P, H, D)
+    full = to_bf16(sdpa(qg, kg, vg, round_probs=True))
+    S_loc = (qg.shape[1] - T) // P
+    for r in range(P):
+        want = np.concatenate([full[:, :T], full[:, T + r * S_loc:T + (r + 1) * S_loc]], axis=1)
+        _assert_bf16_close(want, ref[r])
+        assert np.array_equal(ref[r][:, :T], ref[0][:, :T])
