@@ -230,6 +230,16 @@ def gen_attention():
     kx, vx = seeded((1, 77, 2, 128), 76), seeded((1, 77, 2, 128), 77)
     out["cross128_k"], out["cross128_v"] = kx.astype(np.float32), vx.astype(np.float32)
     out["cross128_o"] = ns["local_attention"](q, kx, vx).astype(np.float32)
+    # key padding through the public API: an additive 0 / -inf key bias
+    # (B, 1, 1, Sk) and the boolean-mask form, ragged valid lengths
+    q, k, v = seeded((2, 33, 2, 128), 78), seeded((2, 41, 2, 128), 79), seeded((2, 41, 2, 128), 80)
+    lens = np.array([41, 19], np.int32)
+    valid = np.arange(41)[None, :] < lens[:, None]
+    bias = np.where(valid, 0.0, -np.inf).astype(np.float32)[:, None, None, :]
+    out["keypad_q"], out["keypad_k"], out["keypad_v"] = (x.astype(np.float32) for x in (q, k, v))
+    out["keypad_len"] = lens
+    out["keypad_o_bias"] = ns["dot_product_attention"](q, k, v, bias=bias).astype(np.float32)
+    out["keypad_o_mask"] = ns["dot_product_attention"](q, k, v, mask=valid[:, None, None, :]).astype(np.float32)
     # Ulysses over P emulated devices, each holding its chunk_by_rank share
     for P, (B, S, H, D) in ((2, (1, 16, 4, 8)), (4, (2, 24, 8, 8)), (8, (1, 256, 8, 128))):
         coll = _Collective(P)

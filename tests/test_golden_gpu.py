@@ -47,6 +47,23 @@ def test_attention_kernel_vs_reference_code():
 
 
 @pytest.mark.gpu
+def test_key_padding_vs_reference_code():
+    """dot_product_attention with a (B, 1, 1, Sk) 0 / -inf key bias and with
+    the boolean mask form, ragged valid lengths (41 and 19 of 41 keys)."""
+    import vidax_b200 as vx
+    g = np.load(os.path.join(GOLDEN, "attention_reference.npz"))
+    q, k, v = _dev(g["keypad_q"]), _dev(g["keypad_k"]), _dev(g["keypad_v"])
+    lens = torch.from_numpy(g["keypad_len"]).long()
+    valid = torch.arange(k.shape[1])[None, :] < lens[:, None]
+    bias = torch.zeros(valid.shape).masked_fill(~valid, float("-inf"))[:, None, None, :]
+    for kw, ref in ((dict(bias=bias.cuda()), g["keypad_o_bias"]),
+                    (dict(mask=valid[:, None, None, :].cuda()), g["keypad_o_mask"])):
+        out = vx.dot_product_attention(q, k, v, **kw)
+        mx, mean = compare(out.float().cpu().numpy(), ref)
+        assert mx <= MAX_ABS and mean <= MEAN_ABS, (list(kw), mx, mean)
+
+
+@pytest.mark.gpu
 def test_ulysses_kernels_vs_reference_code():
     """P=8 Ulysses (1, 256, 8, 128): pack -> (chunk copies standing in for the
     NCCL all-to-all) -> attention -> unpack, per emulated rank, against the

@@ -153,3 +153,13 @@ def test_joint_ulysses_matches_reference_code(attn_gold, P):
         want = np.concatenate([full[:, :T], full[:, T + r * S_loc:T + (r + 1) * S_loc]], axis=1)
         _assert_bf16_close(want, ref[r])
         assert np.array_equal(ref[r][:, :T], ref[0][:, :T])
+
+
+def test_key_padding_matches_reference_code(attn_gold):
+    """dot_product_attention with a 0 / -inf key bias and with the boolean
+    mask form, ragged valid lengths: the oracle's kv_len restatement."""
+    q, k, v = attn_gold["keypad_q"], attn_gold["keypad_k"], attn_gold["keypad_v"]
+    lens = attn_gold["keypad_len"]
+    got = to_bf16(sdpa(q, k, v, kv_len=lens, round_probs=True))
+    _assert_bf16_close(got, attn_gold["keypad_o_bias"])
+    _assert_bf16_close(got, attn_gold["keypad_o_mask"])
