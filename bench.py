@@ -180,6 +180,53 @@ def time_launches(fn, steps: int, warmup: int):
     return e0.elapsed_time(e1) / steps
 
 
+NVLINK_NOMINAL_GBS = 900.0      # per direction per GPU (NVLink 5)
+NVLINK_MEASURED_GBS = 770.0     # peer copy per direction measured on this pool's B200s
+
+
+def measure_all_to_all(numel: int, reps: int, dev, dtype, group=None) -> dict:
+    """One equal-split `all_to_all_single` of `numel` elements per rank (the
+    exchange the Ulysses layer runs four times: q, k, v tokens -> heads and
+    o heads -> tokens), timed `reps` times after 3 warm-up calls: device time
+    with CUDA events on the current stream (wall clock on a CPU group), max
+    over ranks. Bytes per GPU per direction = (P-1)/P of the buffer (the
+    rank's own share does not cross a link)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    numel -= numel % world
+    send = torch.ones(numel, dtype=dtype, device=dev)
+    recv = torch.empty_like(send)
+    for _ in range(3):
+        dist.all_to_all_single(recv, send, group=group)
+    dist.barrier(group=group)
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            dist.all_to_all_single(recv, send, group=group)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+    else:
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            dist.all_to_all_single(recv, send, group=group)
+        ms = (time.perf_counter() - t0) * 1e3 / reps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    ms = float(t.item())
+    link_bytes = (world - 1) / world * numel * send.element_size()
+    gbs = link_bytes / (ms / 1e3) / 1e9
+    return {"buffer_bytes_per_gpu": numel * send.element_size(),
+            "bytes_per_gpu_per_direction": link_bytes, "ms": round(ms, 4),
+            "gbs_per_direction": round(gbs, 1),
+            "frac_of_nvlink_nominal": round(gbs / NVLINK_NOMINAL_GBS, 4),
+            "frac_of_peer_copy_measured": round(gbs / NVLINK_MEASURED_GBS, 4)}
+
+
 def kernel_case(name: str, dev):
     """Named single-kernel cases (profiling and secondary measurements).
 
@@ -500,6 +547,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     elem = 2
     h2d = 3 * B * s_loc * H * D * elem
     d2h = B * s_loc * H * D * elem
+    a2a = None
+    if world > 1:
+        # one q-sized exchange (padded heads) on its own, for the NVLink figure
+        a2a = measure_all_to_all(B * s_loc * (-(-H // world) * world) * D, 10, dev,
+                                 torch.bfloat16)
 
     secondary = {}
     if world == 1 and not args.no_secondary:
@@ -564,7 +616,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if world > 1:
         a2a_bytes = 4 * (world - 1) / world * B * s_loc * hg * world * D * elem
         line["a2a"] = {"bytes_sent_per_gpu": a2a_bytes,
-                       "note": "4 all-to-alls (q, k, v, o) per layer; NVLink 900 GB/s/dir nominal"}
+                       "single_exchange": a2a,
+                       "layer_a2a_ms_if_serial": round(4 * a2a["ms"], 4),
+                       "note": "4 all-to-alls (q, k, v, o) per layer, pipelined by head "
+                               f"slices against the kernel; NVLink {NVLINK_NOMINAL_GBS:.0f} "
+                               f"GB/s/dir nominal, {NVLINK_MEASURED_GBS:.0f} measured peer copy"}
     print(json.dumps(line), flush=True)
 
 

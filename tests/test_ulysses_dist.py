@@ -94,3 +94,44 @@ def test_exchange_matches_tiled_all_to_all(world, H):
         errors.append(errq.get())
     assert not errors, errors
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def _a2a_worker(rank, world, port, errq):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from bench import measure_all_to_all
+        r = measure_all_to_all(1 << 20 | 3, 2, torch.device("cpu"), torch.bfloat16)
+        n = (1 << 20 | 3) - (1 << 20 | 3) % world
+        assert r["buffer_bytes_per_gpu"] == 2 * n
+        assert r["bytes_per_gpu_per_direction"] == (world - 1) / world * 2 * n
+        assert r["ms"] > 0 and r["gbs_per_direction"] > 0
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_bench_all_to_all_measurement_on_gloo():
+    """bench.py's NVLink figure for N > 1: the same collective sequence on
+    every rank, byte accounting of an equal-split exchange."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_a2a_worker, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not errors, errors
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
