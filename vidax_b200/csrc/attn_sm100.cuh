@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float l_sum = 0.f;
       int count = 0;  // KV tiles this query tile processed in this unit
       for (int j = 0; j < n_kv; ++j) {
-        if (!geo.needs(wg, j)) continue;
+        if (!geo.needs_own(j)) continue;
         ok = mbar_wait(bar(kSFull + wg), s_count & 1, abort_flag, status, kDevTimeoutSoftmax);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -500,21 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool need = m_new > m_used + kRescaleThreshold;
         float alpha = 1.f;
         if (need) alpha = ex2_approx(m_used - m_new);  // 0 when m_used = -inf
-        if (count > 0 && __any_sync(0xffffffffu, need)) {
-          // O is complete up to this query tile's previous KV tile: S(j) was
-          // issued after that PV and its commit tracks every earlier MMA.
-          // Rescale this warp's 32 rows of O.
-#pragma unroll 1
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t orr[32];
-            tmem_ld32(t_o + c * 32, orr);
-            tmem_wait_ld(orr);
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-            tmem_st32(t_o + c * 32, orr);
-          }
-        }
+        // O is rescaled after P is computed (fewer live registers) and before P
+        // is published: PV(j) must accumulate into the rescaled O.
+        const bool rescale_o = count > 0 && __any_sync(0xffffffffu, need);
         if (need) {
           l_sum *= alpha;
           m_used = m_new;
@@ -562,6 +550,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           }
           tmem_st16(t_s + c * 16, pk);
+          if (c == (kSplitP ? 1 : 3) && rescale_o) {
+            // O is complete up to this query tile's previous KV tile: S(j) was
+            // issued after that PV and its commit tracks every earlier MMA.
+            // Rescale this warp's 32 rows of O.
+#pragma unroll 1
+            for (int cc = 0; cc < HD / 32; ++cc) {
+              uint32_t orr[32];
+              tmem_ld32(t_o + cc * 32, orr);
+              tmem_wait_ld(orr);
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+              tmem_st32(t_o + cc * 32, orr);
+            }
+          }
           if ((kSplitP && c == 1) || c == 3) {
             tmem_wait_st();
             tc_fence_before();
@@ -654,6 +657,7 @@ struct DenseGeo {
   }
   __device__ int num_kv_tiles() const { return (kv_valid + kBlockN - 1) / kBlockN; }
   __device__ bool needs(int, int) const { return true; }
+  __device__ bool needs_own(int) const { return true; }
   __device__ int last_tile(int) const { return num_kv_tiles() - 1; }
   __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
                          uint64_t pol) const {
@@ -779,6 +783,7 @@ struct NaGeo {
   // softmax row state
   int qc[3];              // query coordinates of this thread's row
   int ws[3];              // window starts
+  int own_lo[3], own_hi[3];  // key union of this thread's query tile
   bool row_valid;
 
   // Work unit u = (region, head, batch), region fastest.
@@ -848,13 +853,29 @@ struct NaGeo {
     o[1] = u0[1] + jh * KH;
     o[2] = u0[2] + jw * KW;
   }
+  // t may be a run-time value (the softmax warpgroup): selects instead of
+  // indexing keep the per-tile arrays in registers.
   __device__ bool needs(int t, int j) const {
     int o[3];
     tile_origin(j, o);
     const int kvb[3] = {KT, KH, KW};
     bool hit = true;
 #pragma unroll
-    for (int a = 0; a < 3; ++a) hit = hit && (o[a] < wu1[t][a]) && (wu0[t][a] < o[a] + kvb[a]);
+    for (int a = 0; a < 3; ++a) {
+      const int lo = t ? wu0[1][a] : wu0[0][a];
+      const int hi = t ? wu1[1][a] : wu1[0][a];
+      hit = hit && (o[a] < hi) && (lo < o[a] + kvb[a]);
+    }
+    return hit;
+  }
+  // needs(t, j) for the query tile softmax_setup was given
+  __device__ bool needs_own(int j) const {
+    int o[3];
+    tile_origin(j, o);
+    const int kvb[3] = {KT, KH, KW};
+    bool hit = true;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) hit = hit && (o[a] < own_hi[a]) && (own_lo[a] < o[a] + kvb[a]);
     return hit;
   }
   __device__ int last_tile(int t) const {
@@ -883,9 +904,14 @@ struct NaGeo {
     const int iw = row % qw;
     const int ih = (row / qw) % qh;
     const int it = row / (qw * qh);
-    qc[0] = org[t][0] + it;
-    qc[1] = org[t][1] + ih;
-    qc[2] = org[t][2] + iw;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      own_lo[a] = t ? wu0[1][a] : wu0[0][a];
+      own_hi[a] = t ? wu1[1][a] : wu1[0][a];
+    }
+    qc[0] = (t ? org[1][0] : org[0][0]) + it;
+    qc[1] = (t ? org[1][1] : org[0][1]) + ih;
+    qc[2] = (t ? org[1][2] : org[0][2]) + iw;
     row_valid = qc[0] < p.T && qc[1] < p.H && qc[2] < p.W;
     const int ksz[3] = {p.kt, p.kh, p.kw};
     const int qg[3] = {min(qc[0], p.T - 1) + p.q_t0, qc[1], qc[2]};  // global query coordinates
