@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               x0 = fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m);
               x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m);
             }
-            if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
+            if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
               e0 = exp2_poly(x0);
               e1 = exp2_poly(x1);
             } else {

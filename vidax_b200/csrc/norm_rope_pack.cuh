@@ -378,7 +378,6 @@ __global__ void __launch_bounds__(kThreads, 1) norm_rope_pack_kernel(
     const __grid_constant__ NormRopeParams p, int* status) {
   extern __shared__ __align__(1024) uint8_t smem[];
   RingControl& ctl = *reinterpret_cast<RingControl*>(smem + p.ctl_off);
-  const HeadSlot* slots = reinterpret_cast<const HeadSlot*>(smem + p.head_off);
   const int S = p.stages;
   const int nslots = p.groups * p.hg;
   // norm weights, rounded to bf16 once (the reference multiplies by
@@ -413,7 +412,6 @@ __global__ void __launch_bounds__(kThreads, 1) norm_rope_pack_kernel(
     if (lane >= kProducerLanes) return;
     const uint64_t policy = l2_policy_evict_first();
     int issued = 0;  // this lane's items issued: n = lane + kProducerLanes * k, k < issued
-    bool ok = true;
     for (int n = lane;; n += kProducerLanes) {
       const int item = blockIdx.x + n * G;
       if (item >= p.items) break;
@@ -421,14 +419,11 @@ __global__ void __launch_bounds__(kThreads, 1) norm_rope_pack_kernel(
       const int round = n / S;
       if (round > 0 &&
           !mbar_wait(smem_u32(&ctl.empty[stage]), static_cast<uint32_t>((round - 1) & 1),
-                     abort_flag, status, kDevTimeoutLoad)) {
-        ok = false;
+                     abort_flag, status, kDevTimeoutLoad))
         break;
-      }
       fill_stage(p, smem, item, stage, smem_u32(&ctl.full[stage]), policy);
       ++issued;
     }
-    (void)ok;
     // Before leaving, wait (bounded) until this lane's fills have landed: if
     // the consumers abort, nothing else would keep the CTA alive while copies
     // into its shared memory are in flight. A fill superseded by a later fill
