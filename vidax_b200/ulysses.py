@@ -274,7 +274,7 @@ def sequence_parallel_self_attention_from_host(
     slab straight into the host output rows (no unpack kernel). Uploads of
     slice j+1 and downloads of slice j-1 run on copy streams while the kernel
     computes slice j."""
-    from .hostio import _check_host, _side_streams
+    from .hostio import _check_host, _side_streams, group_sizes
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check_host(name, t)
     if not (q.shape == k.shape == v.shape):
@@ -289,7 +289,10 @@ def sequence_parallel_self_attention_from_host(
         out = torch.empty((B, S_loc, H, D), dtype=torch.bfloat16).pin_memory()
     Hg = -(-H // P)
     S = P * S_loc
-    sizes = _pieces(Hg)
+    # slices of 1, 2, 4, ... heads and a last one of 1: only the first
+    # slice's upload and the last one's download are not hidden behind a
+    # kernel, and each upload fits under the kernels before it
+    sizes = group_sizes(Hg, 8)
     offs = [sum(sizes[:j]) for j in range(len(sizes))]
     es = 2
     comp = torch.cuda.current_stream(device)
