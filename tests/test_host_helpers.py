@@ -54,3 +54,16 @@ def test_host_attention_head_groups(B, H, Hkv, monkeypatch):
     hostio.attention_from_host(q, k, k.clone(), 0.1, out=torch.empty_like(q), device="cpu")
     assert sum(h for h, _ in seen) == H and sum(g for _, g in seen) == Hkv
     assert all(h == g * (H // Hkv) for h, g in seen)
+
+
+@pytest.mark.parametrize("hkv,cap", [(40, 8), (20, 8), (12, 8), (5, 8), (2, 8), (1, 8), (8, 2), (7, 1)])
+def test_host_group_sizes_ramp(hkv, cap):
+    """Host-buffer pipeline groups: cover every head once, start and end with
+    one head (the exposed upload and download), double up to the cap."""
+    from vidax_b200.hostio import group_sizes
+    sizes = group_sizes(hkv, cap)
+    assert sum(sizes) == hkv and all(1 <= s <= cap for s in sizes)
+    assert sizes[0] == 1 and sizes[-1] == 1
+    body = sizes[:-1] if hkv > 1 else sizes
+    for a, b in zip(body, body[1:]):
+        assert b <= 2 * a  # each upload fits under the kernels before it
