@@ -57,7 +57,8 @@ def test_key_padding_vs_reference_code():
     valid = torch.arange(k.shape[1])[None, :] < lens[:, None]
     bias = torch.zeros(valid.shape).masked_fill(~valid, float("-inf"))[:, None, None, :]
     for kw, ref in ((dict(bias=bias.cuda()), g["keypad_o_bias"]),
-                    (dict(mask=valid[:, None, None, :].cuda()), g["keypad_o_mask"])):
+                    (dict(mask=valid[:, None, None, :].cuda()), g["keypad_o_mask"]),
+                    (dict(mask=valid[:, None, None, :]), g["keypad_o_mask"])):  # host mask
         out = vx.dot_product_attention(q, k, v, **kw)
         mx, mean = compare(out.float().cpu().numpy(), ref)
         assert mx <= MAX_ABS and mean <= MEAN_ABS, (list(kw), mx, mean)

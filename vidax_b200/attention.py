@@ -185,6 +185,8 @@ def dot_product_attention(
         # host tensors: transfers pipelined against the kernel (vidax_b200.hostio)
         from .hostio import attention_from_host
         return attention_from_host(q, k, v, sm_scale, kv_len=kv_len)
+    if kv_len is not None:
+        kv_len = kv_len.to(device=q.device)  # the mask / bias may live on the host
     return flash_attention(q, k, v, sm_scale, kv_len=kv_len)
 
 
