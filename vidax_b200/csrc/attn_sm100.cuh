@@ -361,10 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         Geo geo(p, u);
         const int n = geo.num_kv_tiles();
         if (n == 0) continue;
+        // last tiles first: the scan over the key union runs while Q loads
+        const int last[2] = {geo.last_tile(0), geo.last_tile(1)};
         ok = mbar_wait(bar(kQFull + 0), qi & 1, abort_flag, status, kDevTimeoutMma) &&
              mbar_wait(bar(kQFull + 1), qi & 1, abort_flag, status, kDevTimeoutMma);
         if (!ok) break;
-        const int last[2] = {geo.last_tile(0), geo.last_tile(1)};
         bool first_pv[2] = {true, true};
         tc_fence_after();
 #pragma unroll
@@ -469,6 +470,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int count = 0;  // KV tiles this query tile processed in this unit
       for (int j = 0; j < n_kv; ++j) {
         if (!geo.needs_own(j)) continue;
+        // the tile's key masks need no scores: built while S(j) is computed
+        uint32_t cm[4];
+        const uint32_t active = geo.chunk_masks(j, cm);
         ok = mbar_wait(bar(kSFull + wg), s_count & 1, abort_flag, status, kDevTimeoutSoftmax);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -480,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) pin32(sr[c]);
 
-        const uint32_t active = geo.mask_scores(j, sr);
+        geo.apply_masks(cm, active, sr);
 
         // row max: 3-input max over 128 scores, 4 independent chains
         float mx0 = neg_inf(), mx1 = neg_inf(), mx2 = neg_inf(), mx3 = neg_inf();
@@ -672,18 +676,24 @@ struct DenseGeo {
       tma_load_4d(dst + c * kHalfBytes, tm, bar, 64 * c, hk, j * kBlockN, b, pol);
   }
   __device__ void softmax_setup(int wg, int row) { row_global = q0 + wg * kBlockM + row; }
-  // Masks keys past kv_valid; every 32-column chunk stays active (the
-  // softmax processes all four).
-  __device__ uint32_t mask_scores(int j, uint32_t (&sr)[4][32]) const {
+  // Keys at index >= kv_valid are hidden; every 32-column chunk stays
+  // active (the softmax processes all four). cm[c] bit i: column 32c + i.
+  __device__ uint32_t chunk_masks(int j, uint32_t (&cm)[4]) const {
     const int rem = kv_valid - j * kBlockN;
-    if (rem < kBlockN) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i >= rem) sr[c][i] = 0xff800000u;
+    for (int c = 0; c < 4; ++c) {
+      const int n = rem - c * 32;
+      cm[c] = n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : (1u << n) - 1u);
     }
     return 0xfu;
+  }
+  __device__ void apply_masks(const uint32_t (&cm)[4], uint32_t, uint32_t (&sr)[4][32]) const {
+    if (cm[3] == 0xffffffffu) return;  // full tile (only the last one can be partial)
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (!((cm[c] >> i) & 1u)) sr[c][i] = 0xff800000u;
   }
   __device__ __nv_bfloat16* row_ptr() const {
     return p.o + b * p.o_sb + static_cast<long long>(row_global) * p.o_ss + h * p.o_sh;
@@ -921,10 +931,10 @@ struct NaGeo {
   // Column c of a key tile is key (ct, ch, cw) = (c / (KH*KW), (c / KW) % KH,
   // c % KW) of the tile box; it is visible when each coordinate lies in this
   // row's window. Masks are built per axis as bit fields, then per 32-column
-  // chunk. Returns the chunks (bit c) with a visible column in any row of
-  // this warp: the softmax skips the others (no mask, no exponentials; P is
-  // zero there), which leaves their scores untouched.
-  __device__ uint32_t mask_scores(int j, uint32_t (&sr)[4][32]) const {
+  // chunk (cm[c] bit i: column 32c + i). Returns the chunks (bit c) with a
+  // visible column in any row of this warp: the softmax skips the others (no
+  // mask, no exponentials; P is zero there).
+  __device__ uint32_t chunk_masks(int j, uint32_t (&cm)[4]) const {
     int o[3];
     tile_origin(j, o);
     const uint32_t tmask = bit_range(ws[0] - o[0], ws[0] + p.kt - o[0], KT);
@@ -943,18 +953,26 @@ struct NaGeo {
         if (on) m |= (KW == 32 ? wmask : (wmask << (rr * KW)));
       }
       if (!row_valid) m = 0;
-      if (__any_sync(0xffffffffu, m != 0u)) {
-        active |= 1u << c;
-        if (p.round_logits) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            sr[c][i] = __float_as_uint(__bfloat162float(__float2bfloat16_rn(__uint_as_float(sr[c][i]))));
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sr[c][i] = ((m >> i) & 1u) ? sr[c][i] : 0xff800000u;
-      }
+      cm[c] = m;
+      if (__any_sync(0xffffffffu, m != 0u)) active |= 1u << c;
     }
     return active;
+  }
+  // Hidden columns of the active chunks become -inf (after the optional bf16
+  // rounding of q.k); inactive chunks are left as they are.
+  __device__ void apply_masks(const uint32_t (&cm)[4], uint32_t active,
+                              uint32_t (&sr)[4][32]) const {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (!((active >> c) & 1u)) continue;
+      if (p.round_logits) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          sr[c][i] = __float_as_uint(__bfloat162float(__float2bfloat16_rn(__uint_as_float(sr[c][i]))));
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sr[c][i] = ((cm[c] >> i) & 1u) ? sr[c][i] : 0xff800000u;
+    }
   }
   __device__ __nv_bfloat16* row_ptr() const {
     return p.o + b * p.o_sb + qc[0] * p.o_st + qc[1] * p.o_sh + qc[2] * p.o_sw +
