@@ -558,7 +558,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         burst_peak = load_peaks()[0]
         for case in ("cfg2", "cfg4"):
             fn, fl, desc = kernel_case(case, dev)
-            kms = time_launches(fn, 5 if case == "cfg2" else 20, 3)
+            # idle a second first: right after the power-capped dense runs a
+            # short launch sequence would still run at their reduced clock
+            torch.cuda.synchronize()
+            time.sleep(1.0)
+            kms = time_launches(fn, 5 if case == "cfg2" else 50, 3)
             tf = fl / (kms / 1e3) / 1e12
             secondary[case] = {"desc": desc, "ms": round(kms, 4), "tflops": round(tf, 2),
                                "frac_of_burst_peak": round(tf / burst_peak, 4)}
@@ -567,6 +571,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         hbm, hbm_src = load_hbm_peak()
         for case in (f"prologue:{S_GLOBAL},{H},1", f"prologue:{S_GLOBAL // 8},{H},8"):
             fn, _, desc = kernel_case(case, dev)
+            torch.cuda.synchronize()
+            time.sleep(1.0)
             kms = time_launches(fn, 20, 3)
             gbs = kernel_case_bytes(case) / (kms / 1e3) / 1e9
             secondary[case] = {"desc": desc, "ms": round(kms, 4), "gbs": round(gbs, 1),
