@@ -298,6 +298,20 @@ def kernel_case(name: str, dev):
     raise SystemExit(f"unknown --kernel-only case {name!r}")
 
 
+def na_case_bytes(name: str) -> float:
+    """Algorithmic HBM bytes of a neighborhood-attention case: q, k, v read
+    once and o written once (bf16). cfg4: 805.1 MB."""
+    if name == "cfg4":
+        t, hh, w, nh, hd = 21, 30, 52, 24, D
+    elif name.startswith("na3d64:"):
+        t, hh, w, nh = (int(x) for x in name.split(":")[1].split(",")[:4])
+        hd = 64
+    else:
+        t, hh, w, nh = (int(x) for x in name.split(":")[1].split(","))
+        hd = D
+    return 4 * t * hh * w * nh * hd * 2
+
+
 def kernel_case_bytes(name: str) -> float:
     """Algorithmic HBM bytes of a prologue case: read q, k, v once (bf16),
     write the packed slabs once (P * Hg heads, padding included), read the
@@ -321,6 +335,8 @@ def run_kernel_only(args):
         rec["gbs"] = round(kernel_case_bytes(args.kernel_only) / (ms / 1e3) / 1e9, 1)
     else:
         rec["tflops"] = round(fl / (ms / 1e3) / 1e12, 2)
+    if args.kernel_only == "cfg4" or args.kernel_only.startswith("na3d"):
+        rec["gbs_algorithmic"] = round(na_case_bytes(args.kernel_only) / (ms / 1e3) / 1e9, 1)
     rec["launches"] = args.steps
     print(json.dumps(rec), flush=True)
 
@@ -566,6 +582,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             tf = fl / (kms / 1e3) / 1e12
             secondary[case] = {"desc": desc, "ms": round(kms, 4), "tflops": round(tf, 2),
                                "frac_of_burst_peak": round(tf / burst_peak, 4)}
+            if case == "cfg4":
+                # below the ridge point: the HBM view (q, k, v read, o written once)
+                gbs = na_case_bytes(case) / (kms / 1e3) / 1e9
+                hbm_peak = load_hbm_peak()[0]
+                secondary[case].update(gbs_algorithmic=round(gbs, 1),
+                                       frac_of_hbm=round(gbs / hbm_peak, 4))
         # the fused pre-attention step (RMSNorm + RoPE + send packing) of this
         # layer, per rank at N = 1 and N = 8: HBM-bound
         hbm, hbm_src = load_hbm_peak()

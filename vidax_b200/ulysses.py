@@ -38,6 +38,7 @@ counts that do not divide P are padded with zero heads.
 from __future__ import annotations
 
 import ctypes
+import threading
 from typing import Dict, Optional
 
 import torch
@@ -47,6 +48,7 @@ from . import _lib
 from .attention import flash_attention
 
 _AXES: Dict[str, Optional["dist.ProcessGroup"]] = {}
+_AXES_LOCK = threading.Lock()
 
 #: When set to a list, (start, end) CUDA events bracketing every attention
 #: kernel launch of the sequence-parallel path are appended to it (kernel-level
@@ -57,19 +59,22 @@ KERNEL_EVENTS: Optional[list] = None
 def register_axis(name: str, group=None) -> None:
     """Binds mesh axis `name` to a torch.distributed process group (None =
     the default world group)."""
-    _AXES[name] = group
+    with _AXES_LOCK:
+        _AXES[name] = group
 
 
 def unregister_axis(name: str) -> None:
-    _AXES.pop(name, None)
+    with _AXES_LOCK:
+        _AXES.pop(name, None)
 
 
 def _group(name: str):
-    if name not in _AXES:
-        raise NameError(
-            f"unbound axis name {name!r}: call vidax_b200.register_axis({name!r}, group) first "
-            "(the analogue of running inside shard_map over a mesh with that axis)")
-    return _AXES[name]
+    with _AXES_LOCK:
+        if name in _AXES:
+            return _AXES[name]
+    raise NameError(
+        f"unbound axis name {name!r}: call vidax_b200.register_axis({name!r}, group) first "
+        "(the analogue of running inside shard_map over a mesh with that axis)")
 
 
 def axis_size(name: str) -> int:
