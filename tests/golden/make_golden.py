@@ -199,7 +199,10 @@ def gen_na3d():
     out["ws_start"] = np.array(starts, np.int32)
     cases = [((1, 3, 5, 7, 2, 16), (3, 3, 5)), ((1, 4, 6, 9, 1, 32), (3, 5, 5)),
              ((2, 2, 3, 4, 1, 8), (5, 9, 9)), ((1, 5, 4, 6, 2, 16), (3, 7, 7)),
-             ((1, 3, 5, 9, 2, 128), (3, 3, 5)), ((1, 4, 7, 10, 1, 128), (5, 9, 9))]
+             ((1, 3, 5, 9, 2, 128), (3, 3, 5)), ((1, 4, 7, 10, 1, 128), (5, 9, 9)),
+             # head_dim 64 with LTX-2.5's decoder windows (diffusion_vae.py:547-553);
+             # T = 2 < kt clamps the time window to the whole grid
+             ((1, 4, 6, 10, 2, 64), (3, 5, 5)), ((1, 2, 9, 9, 1, 64), (3, 7, 7))]
     for i, (shape, kernel) in enumerate(cases):
         q = seeded(shape, 40 + i, scale=shape[-1] ** -0.5)
         k = seeded(shape, 50 + i)

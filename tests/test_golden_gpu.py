@@ -22,7 +22,7 @@ def _dev(x):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("i", [4, 5])
+@pytest.mark.parametrize("i", [4, 5, 6, 7])
 @pytest.mark.parametrize("round_logits", [False, True])
 def test_na3d_kernel_vs_reference_code(i, round_logits):
     import vidax_b200 as vx

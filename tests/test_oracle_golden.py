@@ -42,7 +42,7 @@ def test_window_start_bit_exact(na_gold):
         assert np.array_equal(window_start(int(L), int(k)), st[:L]), (L, k)
 
 
-@pytest.mark.parametrize("i", range(6))
+@pytest.mark.parametrize("i", range(8))
 def test_na3d_oracle_matches_reference_code(na_gold, i):
     q, k, v = (na_gold[f"na{i}_{n}"] for n in "qkv")
     kernel = tuple(int(x) for x in na_gold[f"na{i}_kernel"])
