@@ -61,23 +61,6 @@ struct Dims {
   static constexpr uint32_t kTmemO = 256;                        // O_t at kTmemO + HD * t
 };
 
-// Softmax tuning knobs (compile-time): every kPolyEvery-th pair of
-// exponentials goes through the FMA-pipe polynomial (0 = all on MUFU);
-// kSplitP publishes P in two key halves so PV starts on the first half.
-#ifndef VX_POLY_EVERY
-#define VX_POLY_EVERY 0
-#endif
-#ifndef VX_SPLIT_P
-#define VX_SPLIT_P 0
-#endif
-#ifndef VX_PACKED_F32X2
-#define VX_PACKED_F32X2 0
-#endif
-constexpr int kPolyEvery = VX_POLY_EVERY;
-constexpr bool kSplitP = VX_SPLIT_P != 0;
-constexpr bool kPackedF32x2 = VX_PACKED_F32X2 != 0;
-
-
 // barrier slots
 enum : int {
   kQFull = 0,      // 2: [0] = Q0 + the unit's first K, [1] = Q1
@@ -86,15 +69,14 @@ enum : int {
   kKEmpty = 5,     // kStages
   kVEmpty = 7,     // kStages
   kSFull = 9,      // 2
-  kPLo = 11,       // 2: P columns for keys [0, 64) written (split publication)
-  kPHi = 13,       // 2: all P columns written
-  kOFull = 15,     // 2: the unit's last PV of query tile t completed
-  kOFree = 17,     // 2: the epilogue has read O_t
-  kDrain = 19,     // 1
-  kUnitFull = 20,  // 2: unit ring slot written by the scheduler
-  kUnitEmpty = 22, // 2: unit ring slot read by the MMA issuer and all softmax threads
-  kClc = 24,       // 1: cluster-launch-control response landed
-  kNumBars = 25,
+  kPFull = 11,     // 2: all P columns of query tile t written
+  kOFull = 13,     // 2: the unit's last PV of query tile t completed
+  kOFree = 15,     // 2: the epilogue has read O_t
+  kDrain = 17,     // 1
+  kUnitFull = 18,  // 2: unit ring slot written by the scheduler
+  kUnitEmpty = 20, // 2: unit ring slot read by the MMA issuer and all softmax threads
+  kClc = 22,       // 1: cluster-launch-control response landed
+  kNumBars = 23,
 };
 // control block (offsets from the barrier base, which is 1024-aligned)
 constexpr uint32_t kTmemSlotOff = 8 * kNumBars;
@@ -131,8 +113,7 @@ __device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint64_t q_desc, uint6
 // and V an N-major 128B-swizzled tile (`v_desc`): 16 keys per step = 2048
 // bytes; the two 64-column halves of head_dim are kHalfBytes apart (leading
 // byte offset). `half` selects keys [0, 64) or [64, 128) of the tile (4 MMAs
-// each), so the first half can run while the softmax still produces the
-// second.
+// each).
 template <int HD>
 __device__ __forceinline__ void issue_pv_half(uint32_t tmem_o, uint32_t tmem_p, uint64_t v_desc,
                                               int half, bool accumulate) {
@@ -189,8 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kSFull + t), 1);
-      mbar_init(bar(kPLo + t), 128);
-      mbar_init(bar(kPHi + t), 128);
+      mbar_init(bar(kPFull + t), 128);
       mbar_init(bar(kOFull + t), 1);
       mbar_init(bar(kOFree + t), 128);
     }
@@ -401,22 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
               }
-              const uint32_t par = p_count[t] & 1;
-              if (kSplitP) {
-                if (!mbar_wait(bar(kPLo + t), par, abort_flag, status, kDevTimeoutMma)) {
-                  ok = false;
-                  break;
-                }
-                tc_fence_after();
-                issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
-              }
-              if (!mbar_wait(bar(kPHi + t), par, abort_flag, status, kDevTimeoutMma)) {
+              if (!mbar_wait(bar(kPFull + t), p_count[t] & 1, abort_flag, status,
+                             kDevTimeoutMma)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              if (!kSplitP)
-                issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
+              issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
               issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 1, true);
               first_pv[t] = false;
               ++p_count[t];
@@ -512,11 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_used = m_new;
         }
         const float neg_m = (m_used == neg_inf()) ? 0.f : -m_used;
-        // p = 2^(s * scale_log2 - m); optionally one pair in kPolyEvery goes
-        // through the FMA-pipe polynomial instead of MUFU ex2.
-        const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
-        const uint64_t negm2 = f2_pack(neg_m, neg_m);
-        uint64_t lsum2 = f2_pack(0.f, 0.f);
+        // p = 2^(s * scale_log2 - m) on MUFU, packed to bf16 over S's columns
         float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -526,56 +493,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 16; ++i) pk[i] = 0u;
           } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float x0, x1, e0, e1;
-            if (kPackedF32x2) {
-              const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c][2 * i]),
-                                                 __uint_as_float(sr[c][2 * i + 1])),
-                                         scale2, negm2);
-              f2_unpack(x2, x0, x1);
-            } else {
-              x0 = fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m);
-              x1 = fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m);
-            }
-            if (kPolyEvery > 0 && (i % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
-              e0 = exp2_poly(x0);
-              e1 = exp2_poly(x1);
-            } else {
-              e0 = ex2_approx(x0);
-              e1 = ex2_approx(x1);
-            }
-            if (kPackedF32x2) {
-              lsum2 = f2_add(lsum2, f2_pack(e0, e1));
-            } else {
+            for (int i = 0; i < 16; ++i) {
+              const float e0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), scale_log2, neg_m));
+              const float e1 =
+                  ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), scale_log2, neg_m));
               ls0 += e0;
               ls1 += e1;
+              pk[i] = pack_bf16x2(e0, e1);
             }
-            pk[i] = pack_bf16x2(e0, e1);
-          }
           }
           tmem_st16(t_s + c * 16, pk);
-          if (c == (kSplitP ? 1 : 3) && rescale_o) {
-            // O is complete up to this query tile's previous KV tile: S(j) was
-            // issued after that PV and its commit tracks every earlier MMA.
-            // Rescale this warp's 32 rows of O.
+        }
+        if (rescale_o) {
+          // O is complete up to this query tile's previous KV tile: S(j) was
+          // issued after that PV and its commit tracks every earlier MMA.
+          // Rescale this warp's 32 rows of O.
 #pragma unroll 1
-            for (int cc = 0; cc < HD / 32; ++cc) {
-              uint32_t orr[32];
-              tmem_ld32(t_o + cc * 32, orr);
-              tmem_wait_ld(orr);
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            uint32_t orr[32];
+            tmem_ld32(t_o + cc * 32, orr);
+            tmem_wait_ld(orr);
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-              tmem_st32(t_o + cc * 32, orr);
-            }
-          }
-          if ((kSplitP && c == 1) || c == 3) {
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bar((c == 1 ? kPLo : kPHi) + wg));
+            for (int i = 0; i < 32; ++i)
+              orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+            tmem_st32(t_o + cc * 32, orr);
           }
         }
-        if (kPackedF32x2) f2_unpack(lsum2, ls0, ls1);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(kPFull + wg));
         l_sum += ls0 + ls1;
         ++s_count;
         ++count;

@@ -326,27 +326,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe (x <= ~16): round-to-nearest split x = n + f with the
-// 1.5*2^23 shifter, f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted
-// here by relative-error least squares on Chebyshev nodes of [-0.5, 0.5]
-// (iteratively reweighted toward minimax; max relative error 7.5e-5, far below
-// the bf16 rounding the result goes through); n is added to the exponent
-// field with one integer multiply-add. Inputs below -126 are clamped (the
-// result is then a denormal ~0).
-__device__ __forceinline__ float exp2_poly(float x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.9999280571937561f, c1 = 0.6932609677314758f;
-  constexpr float c2 = 0.2426111251115799f, c3 = 0.0551716648042202f;
-  x = fmaxf(x, -126.0f);
-  const float t = x + kShift;
-  const float j = t - kShift;
-  const float f = x - j;
-  float pl = fmaf(c3, f, c2);
-  pl = fmaf(pl, f, c1);
-  pl = fmaf(pl, f, c0);
-  return __int_as_float(__float_as_int(t) * 8388608 + __float_as_int(pl));
-}
-
 // Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions).
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
   uint64_t r;
