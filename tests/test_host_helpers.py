@@ -67,3 +67,31 @@ def test_host_group_sizes_ramp(hkv, cap):
     body = sizes[:-1] if hkv > 1 else sizes
     for a, b in zip(body, body[1:]):
         assert b <= 2 * a  # each upload fits under the kernels before it
+
+
+def test_key_lengths_from_mask_and_bias():
+    """The key-padding forms dot_product_attention accepts become per-batch
+    valid lengths; anything that is not a valid-prefix key mask is refused."""
+    from vidax_b200.attention import _key_lengths_from_bias, _key_lengths_from_mask
+    B, Sk = 3, 7
+    lens = torch.tensor([7, 3, 0])
+    valid = torch.arange(Sk)[None, :] < lens[:, None]
+    for m in (valid[:, None, None, :], valid[:, None, None, :].int()):
+        assert torch.equal(_key_lengths_from_mask(m, B, Sk), lens.int())
+    # one row broadcast over the batch
+    assert torch.equal(_key_lengths_from_mask(valid[1][None, None, None, :], B, Sk),
+                       torch.tensor([3, 3, 3], dtype=torch.int32))
+    bias = torch.zeros(B, 1, 1, Sk).masked_fill(~valid[:, None, None, :], float("-inf"))
+    assert torch.equal(_key_lengths_from_bias(bias, B, Sk), lens.int())
+    big_neg = torch.zeros(B, 1, 1, Sk).masked_fill(~valid[:, None, None, :], -1e30)
+    assert torch.equal(_key_lengths_from_bias(big_neg, B, Sk), lens.int())
+    holes = valid.clone()
+    holes[0, 2] = False  # a hole inside the prefix
+    with pytest.raises(NotImplementedError):
+        _key_lengths_from_mask(holes[:, None, None, :], B, Sk)
+    with pytest.raises(NotImplementedError):  # per-query (dense) mask
+        _key_lengths_from_mask(torch.ones(B, 1, 5, Sk, dtype=torch.bool), B, Sk)
+    with pytest.raises(NotImplementedError):  # dense additive bias (T5-style)
+        _key_lengths_from_bias(torch.zeros(B, 2, 5, Sk), B, Sk)
+    with pytest.raises(NotImplementedError):  # values other than 0 / -inf
+        _key_lengths_from_bias(torch.full((B, 1, 1, Sk), -3.0), B, Sk)
