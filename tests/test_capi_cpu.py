@@ -99,3 +99,68 @@ def test_norm_rope_pack_validation_without_device(lib):
     a.seq = 0
     a.src[0] = a.dst[0] = 4096
     assert lib.vx_norm_rope_pack(ctypes.byref(a), None) == _lib.VX_OK     # empty: no launch
+
+
+def test_na3d_validation_without_device(lib):
+    from vidax_b200 import _lib
+    from vidax_b200.neighborhood import Na3dArgs, Na3dSlab
+    fn = lib.vx_na3d_fwd
+    fn.argtypes = [ctypes.POINTER(Na3dArgs), ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    slab_fn = lib.vx_na3d_fwd_slab
+    slab_fn.argtypes = [ctypes.POINTER(Na3dArgs), ctypes.POINTER(Na3dSlab), ctypes.c_void_p]
+    slab_fn.restype = ctypes.c_int
+    assert fn(None, None) == _lib.VX_EINVAL
+    a = Na3dArgs()
+    a.batch, a.T, a.H, a.W, a.heads, a.heads_kv, a.head_dim = 1, 3, 4, 5, 2, 2, 128
+    a.kernel_t, a.kernel_h, a.kernel_w, a.scale = 3, 3, 3, 1.0
+    a.heads_kv = 3                                   # 2 % 3 != 0
+    assert fn(ctypes.byref(a), None) == _lib.VX_EINVAL
+    a.heads_kv, a.kernel_h = 2, 0
+    assert fn(ctypes.byref(a), None) == _lib.VX_EINVAL
+    assert b"kernel" in lib.vx_last_error()
+    a.kernel_h, a.head_dim = 3, 96
+    assert fn(ctypes.byref(a), None) == _lib.VX_EUNSUPPORTED
+    a.head_dim, a.scale = 64, 0.0
+    assert fn(ctypes.byref(a), None) == _lib.VX_EUNSUPPORTED
+    a.scale, a.T = 1.0, 0
+    assert fn(ctypes.byref(a), None) == _lib.VX_OK    # empty grid: no launch
+    a.T = 3
+    assert fn(ctypes.byref(a), None) == _lib.VX_EINVAL  # o is NULL
+    assert slab_fn(ctypes.byref(a), None, None) == _lib.VX_EINVAL
+
+
+def test_glue_and_copy_validation_without_device(lib):
+    from vidax_b200 import _lib
+    null = ctypes.c_void_p(None)
+    i64, i32 = ctypes.c_int64, ctypes.c_int32
+
+    def ln(rows, dim, rpb, x=None, y=None, w=None, b=None):
+        return lib.vx_ln_modulate(ctypes.c_void_p(x), ctypes.c_void_p(y), ctypes.c_void_p(w),
+                                  ctypes.c_void_p(b), null, null, i64(rows), i32(dim), i32(rpb),
+                                  ctypes.c_float(1e-6), null)
+    assert ln(8, 6, 8) == _lib.VX_EINVAL            # dim not a multiple of 4
+    assert ln(8, 8, 3) == _lib.VX_EINVAL            # rows not a multiple of rows_per_batch
+    assert ln(0, 8, 1) == _lib.VX_OK                # empty: no launch
+    assert ln(8, 8, 8) == _lib.VX_EINVAL            # x / y NULL
+    assert ln(8, 8, 8, x=4096, y=8192, w=4096) == _lib.VX_EINVAL  # w without b
+    assert ln(8, 8, 8, x=4100, y=8192) == _lib.VX_EINVAL          # misaligned x
+
+    def gr(rows, dim, rpb, x=None, y=None):
+        return lib.vx_gated_residual(ctypes.c_void_p(x), ctypes.c_void_p(y), null, i64(rows),
+                                     i32(dim), i32(rpb), null)
+    assert gr(8, 12, 8) == _lib.VX_EINVAL           # dim not a multiple of 8
+    assert gr(0, 8, 1) == _lib.VX_OK
+    assert gr(8, 8, 8) == _lib.VX_EINVAL            # NULL
+    assert gr(8, 8, 8, x=4112, y=8192) == _lib.VX_EINVAL  # x not 32-byte aligned
+
+    cp = lib.vx_memcpy_rows_async
+    assert cp(None, 0, None, 0, 0, 5, None) == _lib.VX_OK       # nothing to copy
+    assert cp(None, 64, None, 64, 64, 5, None) == _lib.VX_EINVAL
+    assert cp(4096, 32, 8192, 64, 64, 5, None) == _lib.VX_EINVAL  # dst pitch < row bytes
+
+    st = lib.vx_selftest_wait_timeout
+    st.argtypes = [ctypes.c_int64, ctypes.POINTER(ctypes.c_int)]
+    st.restype = ctypes.c_int
+    assert st(0, None) == _lib.VX_EINVAL
+    assert st(5_000_000_000, None) == _lib.VX_EINVAL
