@@ -95,3 +95,19 @@ def test_key_lengths_from_mask_and_bias():
         _key_lengths_from_bias(torch.zeros(B, 2, 5, Sk), B, Sk)
     with pytest.raises(NotImplementedError):  # values other than 0 / -inf
         _key_lengths_from_bias(torch.full((B, 1, 1, Sk), -3.0), B, Sk)
+
+
+def test_host_paths_reject_a_wrong_out_buffer():
+    """The host-buffer paths copy device rows straight into `out`: a buffer of
+    another shape, dtype or row layout is refused before any device work."""
+    from vidax_b200.hostio import attention_from_host
+    from vidax_b200.ulysses import sequence_parallel_self_attention_from_host
+    q = torch.zeros(1, 8, 2, 64, dtype=torch.bfloat16)
+    dev = torch.device("cuda", 0)  # never reached: validation comes first
+    for bad, err in ((torch.zeros(1, 4, 2, 64, dtype=torch.bfloat16), ValueError),
+                     (torch.zeros(1, 8, 2, 64), NotImplementedError),
+                     (torch.zeros(1, 8, 64, 2, dtype=torch.bfloat16).transpose(2, 3), ValueError)):
+        with pytest.raises(err):
+            attention_from_host(q, q, q, 0.125, out=bad, device=dev)
+        with pytest.raises(err):
+            sequence_parallel_self_attention_from_host(q, q, q, "sp", out=bad, device=dev)

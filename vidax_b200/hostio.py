@@ -74,6 +74,14 @@ def _check_host(name: str, t: torch.Tensor) -> None:
         raise ValueError(f"{name} must be (B, S, H, D) with contiguous (H, D) rows")
 
 
+def check_host_out(out: torch.Tensor, shape) -> None:
+    """`out` receives row copies straight from the device: it must be a host
+    bf16 tensor of exactly `shape` with contiguous (H, D) rows."""
+    _check_host("out", out)
+    if tuple(out.shape) != tuple(shape):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {tuple(shape)}")
+
+
 def attention_from_host(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
     kv_len: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
@@ -103,6 +111,8 @@ def attention_from_host(
         sizes = [min(n, Hkv - i) for i in range(0, Hkv, n)]
     if out is None:
         out = torch.empty((B, Sq, H, D), dtype=torch.bfloat16).pin_memory()
+    else:
+        check_host_out(out, (B, Sq, H, D))
     qd = torch.empty((B, Sq, H, D), dtype=torch.bfloat16, device=device)
     kd = torch.empty((B, Sk, Hkv, D), dtype=torch.bfloat16, device=device)
     vd = torch.empty_like(kd)

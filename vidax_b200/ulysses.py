@@ -279,11 +279,13 @@ def sequence_parallel_self_attention_from_host(
     slab straight into the host output rows (no unpack kernel). Uploads of
     slice j+1 and downloads of slice j-1 run on copy streams while the kernel
     computes slice j."""
-    from .hostio import _check_host, _side_streams, group_sizes
+    from .hostio import _check_host, _side_streams, check_host_out, group_sizes
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check_host(name, t)
     if not (q.shape == k.shape == v.shape):
         raise ValueError("self-attention needs q, k, v of equal shape")
+    if out is not None:
+        check_host_out(out, q.shape)
     group = _group(sp_axis_name)
     P = dist.get_world_size(group)
     B, S_loc, H, D = q.shape
