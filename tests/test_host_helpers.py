@@ -111,3 +111,18 @@ def test_host_paths_reject_a_wrong_out_buffer():
             attention_from_host(q, q, q, 0.125, out=bad, device=dev)
         with pytest.raises(err):
             sequence_parallel_self_attention_from_host(q, q, q, "sp", out=bad, device=dev)
+
+
+def test_slab_calls_check_buffers_before_the_kernel():
+    """pack / unpack refuse packed buffers of the wrong size (the kernel would
+    write past them) and views of the wrong shape, before any launch."""
+    from vidax_b200.ulysses import pack_heads, unpack_heads
+    x = torch.zeros(6, 10, 64, dtype=torch.bfloat16)     # (S_loc, H, D)
+    with pytest.raises(ValueError, match="packed buffer"):
+        pack_heads([x], 4, out=[torch.zeros(4, 6, 2, 64, dtype=torch.bfloat16)])  # Hg = 3
+    with pytest.raises(ValueError, match="packed buffer"):
+        unpack_heads([torch.zeros(4, 6, 3, 64, dtype=torch.bfloat16)], [x], 10, sub=(2, 3, 0, 2))
+    with pytest.raises(ValueError, match="view"):
+        unpack_heads([torch.zeros(4, 6, 3, 64, dtype=torch.bfloat16)], [x], 12)
+    with pytest.raises(ValueError, match="CUDA"):        # right sizes, host memory
+        pack_heads([x], 4, out=[torch.zeros(4, 6, 3, 64, dtype=torch.bfloat16)])

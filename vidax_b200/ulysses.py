@@ -110,10 +110,23 @@ def _slab_call(fn_name: str, strided, packed, heads: int, groups: int, sub=None)
     head_offset, group_valid) selects a sub-group of every group."""
     a = HeadSlabArgs()
     a.num_tensors = len(strided)
+    if not 1 <= len(strided) <= 3 or len(packed) != len(strided):
+        raise ValueError("1 to 3 tensors, one packed buffer each")
     seq, _, d = strided[0].shape
+    hg = sub[0] if sub is not None and any(sub) else -(-heads // groups)
+    want = groups * seq * hg * d   # the kernel writes / reads exactly this many elements
+    dev = strided[0].device
     for i, (s_t, p_t) in enumerate(zip(strided, packed)):
-        if not p_t.is_contiguous():
-            raise ValueError("packed side must be contiguous")
+        if tuple(s_t.shape) != (seq, heads, d):
+            raise ValueError(f"tensor {i}: expected a ({seq}, {heads}, {d}) view, got "
+                             f"{tuple(s_t.shape)}")
+        if not p_t.is_contiguous() or p_t.numel() != want:
+            raise ValueError(f"packed buffer {i} must be contiguous with {groups} x {seq} x "
+                             f"{hg} x {d} elements")
+        if s_t.element_size() != 2 or p_t.dtype != s_t.dtype:
+            raise NotImplementedError("the slab kernels move 16-bit elements (bf16)")
+        if not s_t.is_cuda or s_t.device != dev or p_t.device != dev:
+            raise ValueError("all tensors must live on the same CUDA device")
         if s_t.stride(-1) != 1:
             raise ValueError("head_dim must be contiguous")
         if fn_name == "vx_ulysses_pack":
