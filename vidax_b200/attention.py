@@ -76,12 +76,14 @@ def flash_attention(
     q, k, v = _tma_ready(q), _tma_ready(k), _tma_ready(v)
     if out is None:
         out = torch.empty((B, Sq, Hq, D), dtype=torch.bfloat16, device=q.device)
-    elif out.shape != (B, Sq, Hq, D) or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
-        raise ValueError("out must be a bf16 (B, Sq, Hq, D) tensor with contiguous head_dim")
+    elif (out.shape != (B, Sq, Hq, D) or out.dtype != torch.bfloat16 or out.stride(-1) != 1
+          or out.device != q.device):
+        raise ValueError("out must be a bf16 (B, Sq, Hq, D) tensor with contiguous head_dim "
+                         "on q's device")
     lse = torch.empty((B, Hq, Sq), dtype=torch.float32, device=q.device) if return_lse else None
     if kv_len is not None:
-        if kv_len.dtype != torch.int32 or kv_len.numel() != B or not kv_len.is_cuda:
-            raise ValueError("kv_len must be an int32 CUDA tensor with B elements")
+        if kv_len.dtype != torch.int32 or kv_len.numel() != B or kv_len.device != q.device:
+            raise ValueError("kv_len must be an int32 tensor with B elements on q's device")
         kv_len = kv_len.contiguous()
 
     a = _lib.AttnArgs()

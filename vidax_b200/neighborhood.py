@@ -114,6 +114,8 @@ def neighborhood_attention_3d_slab(
 def _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, slab):
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check6(name, t)
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must live on the same device")
     B, T, H, W, NH, HD = q.shape
     kv_frames = k.shape[1] if slab is not None else T
     if (k.shape[0] != B or k.shape[1] != kv_frames or k.shape[2:4] != q.shape[2:4]

@@ -161,8 +161,10 @@ def norm_rope_pack(
     keep = []
     ncols = D if per_head else heads * D
     for i, (r, o) in enumerate(zip(rows, out)):
-        if not o.is_contiguous() or o.numel() != B * groups * S * hg * D:
-            raise ValueError("out buffers must be contiguous with B*groups*S*Hg*D elements")
+        if (not o.is_contiguous() or o.numel() != B * groups * S * hg * D
+                or o.dtype != torch.bfloat16 or o.device != x0.device):
+            raise ValueError("out buffers must be contiguous bf16 with B*groups*S*Hg*D "
+                             "elements on the inputs' device")
         a.src[i], a.dst[i] = r.data_ptr(), o.data_ptr()
         for k in range(3):
             a.src_stride[i][k] = r.stride(k)
