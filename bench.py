@@ -17,7 +17,9 @@ One JSON line (rank 0): value = whole-job attention TFLOP/s (vidax's FLOP
 convention 4*B*H*S*S*D over the max-over-ranks step time), `e2e` = the same
 through the public API with pinned host inputs copied in and the output
 copied out every step, `roofline` = the attention kernel against the
-measured bf16 peak, `cpu_baseline` = the CPU oracle on a bounded sample.
+measured bf16 peak, `cpu_baseline` = the CPU oracle on a bounded sample;
+`secondary` (N=1) = cfg2, cfg4 and fused pre-step kernel timings, and the
+numpy restatement of vidax's NA scan timed on cfg4 row steps.
 
 `--impl reference` times the reference's CPU path (vidax's JAX CPU attention
 is `jax.nn.dot_product_attention`; JAX is absent, so its numpy restatement in
@@ -140,17 +142,22 @@ def gpu_id_for(dev) -> str:
         return str(dev)
 
 
+def blas_threads() -> int:
+    """Threads numpy's BLAS runs with (the host cores a CPU baseline uses)."""
+    try:
+        from threadpoolctl import threadpool_info
+        return max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:
+        return os.cpu_count()
+
+
 def cpu_sample(seconds: float, rows_per_chunk: int = 256):
     """Times the oracle (numpy restatement of jax.nn.dot_product_attention) on
     head 0 of the workload: chunks of query rows against all S keys, until
     `seconds` of CPU time have run. Returns (TFLOP/s, threads, description)."""
     import numpy as np
     from oracle.attention_ref import sdpa, seeded_qkv
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:
-        threads = os.cpu_count()
+    threads = blas_threads()
     q, k, v = seeded_qkv((1, S_GLOBAL, 1, D), 3)
     done_rows, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds and done_rows < S_GLOBAL:
@@ -162,6 +169,36 @@ def cpu_sample(seconds: float, rows_per_chunk: int = 256):
     desc = (f"numpy oracle, head 0 of cfg3: {done_rows} query rows x {S_GLOBAL} keys "
             f"({flops(1, 1, done_rows, S_GLOBAL, D) / 1e9:.1f} GFLOP in {dt:.1f} s)")
     return tf, threads, desc
+
+
+def na_cpu_sample(seconds: float):
+    """Times the oracle's restatement of vidax's NA scan step (one (t, h) row
+    of diffusion_vae.py:206-225: gather the row's 5x9 frame/row windows, the
+    W-window of every w, two einsums) for cfg4's shapes: W = 52, 24 heads,
+    head_dim 128, window 5x9x9. Every cfg4 row does the same work (windows
+    shift at the borders, they do not shrink), so the rows are timed on the
+    centre row of a 5 x 9 x 52 grid, whose window is that whole grid, and the
+    full scan is the per-row time x 630 rows. Returns a secondary-line dict."""
+    import numpy as np
+    from oracle.attention_ref import to_bf16
+    from oracle.na3d_ref import na3d
+    kernel, rows_full = (5, 9, 9), 21 * 30
+    shape = (1, 5, 9, 52, 24, D)
+    rng = np.random.Generator(np.random.PCG64(4))
+    q = to_bf16(to_bf16(rng.standard_normal(shape, dtype=np.float32)) * D ** -0.5)
+    k = to_bf16(rng.standard_normal(shape, dtype=np.float32))
+    v = to_bf16(rng.standard_normal(shape, dtype=np.float32))
+    na3d(q, k, v, kernel, round_logits=True, round_probs=True, rows=[(2, 4)])  # warm-up
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        na3d(q, k, v, kernel, round_logits=True, round_probs=True, rows=[(2, 4)])
+        done += 1
+    dt = time.perf_counter() - t0
+    row_flops = 4.0 * 52 * 405 * D * 24
+    return {"desc": f"numpy restatement of vidax's NA scan, cfg4 row steps: {done} rows in "
+                    f"{dt:.1f} s (the full scan is 630 rows)", "rows": done,
+            "est_full_ms": round(dt / done * rows_full * 1e3, 1),
+            "tflops": round(row_flops * done / dt / 1e12, 5), "cores": blas_threads()}
 
 
 def time_launches(fn, steps: int, warmup: int):
@@ -411,11 +448,7 @@ def run_reference(args, rank: int):
         return
     import numpy as np
     from oracle.attention_ref import sdpa, seeded_qkv
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:
-        threads = os.cpu_count()
+    threads = blas_threads()
     q, k, v = seeded_qkv((1, S_GLOBAL, 1, D), 3)
     rows_per_step = 2048
 
@@ -600,6 +633,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             secondary[case] = {"desc": desc, "ms": round(kms, 4), "gbs": round(gbs, 1),
                                "frac_of_hbm": round(gbs / hbm, 4), "hbm_peak_source": hbm_src}
         assert _lib.device_status() == 0
+
+    if secondary and not args.no_cpu_baseline:
+        # vidax's NA on the host cores (its scan restated in numpy), next to
+        # the kernel's cfg4 line
+        na_cpu = na_cpu_sample(args.cpu_seconds / 2)
+        if "cfg4" in secondary:
+            na_cpu["est_full_over_kernel"] = round(na_cpu["est_full_ms"] / secondary["cfg4"]["ms"])
+        secondary["cfg4_cpu_scan"] = na_cpu
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -41,11 +41,14 @@ def window_sets(T: int, H: int, W: int, kernel_size):
     return [(window_start(L, k), k) for L, k in zip((T, H, W), ks)]
 
 
-def na3d(q, k, v, kernel_size, round_logits=False, round_probs=False, positions=None):
+def na3d(q, k, v, kernel_size, round_logits=False, round_probs=False, positions=None,
+         rows=None):
     """q, k, v: (B, T, H, W, NH, HD) float32 (bf16-exact values; q pre-scaled).
 
     Returns float32 (B, T, H, W, NH, HD), or (B, N, NH, HD) for the query
-    `positions` (N, 3) of (t, h, w) when given.
+    `positions` (N, 3) of (t, h, w) when given. `rows` ((t, h) pairs)
+    computes only those scan steps of the full-grid form (the others stay
+    zero): a bounded sample of the reference's per-row work.
     """
     q = np.asarray(q, np.float32)
     k = np.asarray(k, np.float32)
@@ -80,9 +83,9 @@ def na3d(q, k, v, kernel_size, round_logits=False, round_probs=False, positions=
     if positions is None:
         out = np.zeros_like(q)
         all_w = np.arange(W)
-        for t in range(T):
-            for h in range(H):
-                out[:, t, h] = row(t, h, all_w)
+        steps = rows if rows is not None else [(t, h) for t in range(T) for h in range(H)]
+        for t, h in steps:
+            out[:, t, h] = row(int(t), int(h), all_w)
         return out
     positions = np.asarray(positions)
     out = np.zeros((B, len(positions), NH, HD), np.float32)
