@@ -201,6 +201,15 @@ def na_cpu_sample(seconds: float):
             "tflops": round(row_flops * done / dt / 1e12, 5), "cores": blas_threads()}
 
 
+def add_na_cpu_line(secondary: dict, seconds: float) -> None:
+    """vidax's NA on the host cores (its scan restated in numpy) as the
+    `cfg4_cpu_scan` secondary entry, next to the kernel's cfg4 line."""
+    na_cpu = na_cpu_sample(seconds)
+    if "cfg4" in secondary:
+        na_cpu["est_full_over_kernel"] = round(na_cpu["est_full_ms"] / secondary["cfg4"]["ms"])
+    secondary["cfg4_cpu_scan"] = na_cpu
+
+
 def time_launches(fn, steps: int, warmup: int):
     """Device time (ms) per launch of `fn`, CUDA events on the current stream."""
     import torch
@@ -635,12 +644,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         assert _lib.device_status() == 0
 
     if secondary and not args.no_cpu_baseline:
-        # vidax's NA on the host cores (its scan restated in numpy), next to
-        # the kernel's cfg4 line
-        na_cpu = na_cpu_sample(args.cpu_seconds / 2)
-        if "cfg4" in secondary:
-            na_cpu["est_full_over_kernel"] = round(na_cpu["est_full_ms"] / secondary["cfg4"]["ms"])
-        secondary["cfg4_cpu_scan"] = na_cpu
+        add_na_cpu_line(secondary, args.cpu_seconds / 2)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -126,3 +126,16 @@ def test_slab_calls_check_buffers_before_the_kernel():
         unpack_heads([torch.zeros(4, 6, 3, 64, dtype=torch.bfloat16)], [x], 12)
     with pytest.raises(ValueError, match="CUDA"):        # right sizes, host memory
         pack_heads([x], 4, out=[torch.zeros(4, 6, 3, 64, dtype=torch.bfloat16)])
+
+
+def test_bench_na_cpu_line():
+    """bench.py's CPU leg for cfg4: the oracle's scan timed on row steps, the
+    JSON fields the bench line carries."""
+    import json
+    import bench
+    sec = {"cfg4": {"ms": 1.2}}
+    bench.add_na_cpu_line(sec, 0.5)
+    line = sec["cfg4_cpu_scan"]
+    assert line["rows"] >= 1 and line["est_full_ms"] > 0 and line["cores"] >= 1
+    assert line["est_full_over_kernel"] == round(line["est_full_ms"] / 1.2)
+    json.dumps(sec)
