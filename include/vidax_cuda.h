@@ -27,7 +27,7 @@ enum {
   VX_EINVAL = 1,        /* bad argument: shape, stride, alignment, null pointer */
   VX_EUNSUPPORTED = 2,  /* valid request this build does not implement */
   VX_ECUDA = 3,         /* CUDA runtime / driver error */
-  VX_ENCCL = 4,         /* NCCL error */
+  VX_ENCCL = 4,         /* reserved (NCCL error): the library itself calls no collective */
   VX_ETIMEOUT = 5,      /* a bounded device-side wait expired (see vx_device_status) */
 };
 
