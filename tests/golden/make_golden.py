@@ -263,12 +263,14 @@ def gen_attention():
         out[f"sp{P}_q"], out[f"sp{P}_k"], out[f"sp{P}_v"] = (x.astype(np.float32) for x in (qg, kg, vg))
         out[f"sp{P}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
     # joint [text; visual] Ulysses (CogVideoX layout): text replicated, visual chunked
-    for P, (B, T, S, H, D) in ((2, (1, 5, 16, 4, 8)), (4, (2, 7, 24, 8, 8))):
+    # (the head_dim-128 case is the size the sm_100a kernel takes)
+    for tag, P, (B, T, S, H, D) in (("joint2", 2, (1, 5, 16, 4, 8)), ("joint4", 4, (2, 7, 24, 8, 8)),
+                                    ("joint2d128", 2, (1, 13, 80, 4, 128))):
         coll = _Collective(P)
         ns_p = load_functions("src/vidax/core/attention.py",
                               names + ["sequence_parallel_joint_self_attention"],
                               make_namespace(coll))
-        qg, kg, vg = (seeded((B, T + S, H, D), 110 + P + i) for i in range(3))
+        qg, kg, vg = (seeded((B, T + S, H, D), 110 + P + i + (D > 8) * 7) for i in range(3))
         results = [None] * P
         S_loc = S // P
 
@@ -283,9 +285,9 @@ def gen_attention():
             t.start()
         for t in threads:
             t.join()
-        out[f"joint{P}_q"], out[f"joint{P}_k"], out[f"joint{P}_v"] = (x.astype(np.float32) for x in (qg, kg, vg))
-        out[f"joint{P}_text_len"] = np.array([T], np.int32)
-        out[f"joint{P}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
+        out[f"{tag}_q"], out[f"{tag}_k"], out[f"{tag}_v"] = (x.astype(np.float32) for x in (qg, kg, vg))
+        out[f"{tag}_text_len"] = np.array([T], np.int32)
+        out[f"{tag}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
     return out
 
 
