@@ -92,3 +92,81 @@ def test_exchange_halo_delivers_the_key_frames(world, T, kt):
         errors.append(errq.get())
     assert not errors, errors
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def _oracle_slab(q, k_ext, v_ext, kernel_size, *, t_global, q_t0, kv_t0, scale=1.0,
+                 round_logits=False):
+    """The slab kernel's contract restated with the oracle: the slab's rows
+    of the unsharded call, its key frames placed at their global offset
+    (frames outside them must never be read: left as NaN)."""
+    from oracle.na3d_ref import na3d
+    B, T, H, W, NH, HD = q.shape
+    shape = (B, t_global, H, W, NH, HD)
+    qg = np.zeros(shape, np.float32)
+    kg = np.full(shape, np.nan, np.float32)
+    vg = np.full(shape, np.nan, np.float32)
+    qg[:, q_t0:q_t0 + T] = (q * scale).numpy()
+    kg[:, kv_t0:kv_t0 + k_ext.shape[1]] = k_ext.numpy()
+    vg[:, kv_t0:kv_t0 + v_ext.shape[1]] = v_ext.numpy()
+    rows = [(t, h) for t in range(q_t0, q_t0 + T) for h in range(H)]
+    out = na3d(qg, kg, vg, kernel_size, rows=rows)
+    return torch.from_numpy(out[:, q_t0:q_t0 + T].copy())
+
+
+def _sp_worker(rank, world, port, sizes, kernel, pass_t, errq):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        import vidax_b200 as vx
+        from vidax_b200 import na_parallel
+        from oracle.na3d_ref import na3d
+        na_parallel.neighborhood_attention_3d_slab = _oracle_slab
+        vx.register_axis("sp", None)
+        T = sum(sizes)
+        rng = np.random.default_rng(13)
+        qg, kg, vg = (rng.standard_normal((1, T, 4, 6, 2, 8)).astype(np.float32) for _ in range(3))
+        b0 = sum(sizes[:rank])
+        mine = [torch.from_numpy(x[:, b0:b0 + sizes[rank]].copy()) for x in (qg, kg, vg)]
+        out = na_parallel.neighborhood_attention_3d_sp(
+            *mine, kernel, "sp", t_global=T if pass_t else None)
+        ref = na3d(qg, kg, vg, kernel)[:, b0:b0 + sizes[rank]]
+        assert out.shape == ref.shape
+        assert np.isfinite(out.numpy()).all(), "read a key frame outside the exchanged range"
+        assert np.allclose(out.numpy(), ref, atol=1e-5), float(np.abs(out.numpy() - ref).max())
+        vx.unregister_axis("sp")
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # report to the parent
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("sizes,kernel,pass_t", [
+    ((4, 4, 3), (5, 3, 3), True),      # split_sizes(11, 3)
+    ((2, 5, 0, 4), (3, 3, 5), False),  # uneven, one rank without frames: sizes all-gathered
+    ((1, 1, 1, 1), (5, 3, 3), False),  # slabs thinner than the window
+])
+def test_time_sharded_na_matches_unsharded(sizes, kernel, pass_t):
+    """neighborhood_attention_3d_sp end to end on gloo (the slab kernel
+    replaced by the oracle's rows of the global grid): every rank's output
+    equals the same frames of the unsharded attention."""
+    world = len(sizes)
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, list(sizes), kernel, pass_t,
+                                                  errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not errors, errors
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
