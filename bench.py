@@ -142,6 +142,20 @@ def gpu_id_for(dev) -> str:
         return str(dev)
 
 
+def host_cpu() -> dict:
+    """The host the CPU baseline ran on: CPU model and logical core count."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "logical_cpus": os.cpu_count()}
+
+
 def blas_threads() -> int:
     """Threads numpy's BLAS runs with (the host cores a CPU baseline uses)."""
     try:
@@ -483,7 +497,7 @@ def run_reference(args, rank: int):
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample": "bounded CPU sample per step"},
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": sample, **host_cpu()},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -650,7 +664,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, threads, desc = cpu_sample(args.cpu_seconds)
         cpu = {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": desc}
+               "sample": desc, **host_cpu()}
 
     if world > 1:
         vx.unregister_axis("sp")

@@ -139,3 +139,9 @@ def test_bench_na_cpu_line():
     assert line["rows"] >= 1 and line["est_full_ms"] > 0 and line["cores"] >= 1
     assert line["est_full_over_kernel"] == round(line["est_full_ms"] / 1.2)
     json.dumps(sec)
+
+
+def test_bench_host_cpu_record():
+    import bench
+    h = bench.host_cpu()
+    assert set(h) == {"cpu_model", "logical_cpus"} and h["logical_cpus"] >= 1
