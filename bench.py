@@ -287,6 +287,43 @@ def measure_all_to_all(numel: int, reps: int, dev, dtype, group=None) -> dict:
             "frac_of_peer_copy_measured": round(gbs / NVLINK_MEASURED_GBS, 4)}
 
 
+def parity_sample(out, q, k, v, world: int, dev, rows_per_rank: int = 32) -> dict:
+    """Checks seeded rows of the layer's output (this rank's local tokens,
+    all heads) against a float32-softmax attention computed with torch on
+    the GPU over the global sequence (the ranks' k / v gathered when N > 1).
+    Returns the max / mean absolute error over ranks and whether they meet
+    the tolerance (max-abs 2e-2, mean-abs 2e-3)."""
+    import torch
+    import torch.distributed as dist
+    b, s_loc, h, d = q.shape
+    if world > 1:
+        kg = torch.empty((world,) + tuple(k.shape[1:]), dtype=k.dtype, device=dev)
+        vg = torch.empty_like(kg)
+        dist.all_gather_into_tensor(kg, k[0].contiguous())
+        dist.all_gather_into_tensor(vg, v[0].contiguous())
+        kg, vg = kg.reshape(-1, h, d), vg.reshape(-1, h, d)
+    else:
+        kg, vg = k[0], v[0]
+    gen = torch.Generator().manual_seed(11)
+    idx = torch.cat([torch.arange(0, 2), torch.arange(s_loc - 2, s_loc),
+                     torch.randint(0, s_loc, (rows_per_rank - 4,), generator=gen)]).to(dev)
+    logits = torch.einsum("nhd,shd->hns", q[0, idx].float(), kg.float()) * (d ** -0.5)
+    ref = torch.einsum("hns,shd->nhd", torch.softmax(logits, dim=-1), vg.float())
+    del logits
+    diff = (out[0, idx].float() - ref).abs()
+    stats = torch.tensor([diff.max().item(), diff.mean().item()], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = stats[:1].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(stats, op=dist.ReduceOp.SUM)
+        stats = torch.stack([mx[0], stats[1] / world])
+    mx, mean = float(stats[0]), float(stats[1])
+    return {"max_abs": round(mx, 6), "mean_abs": round(mean, 7), "rows_per_rank": rows_per_rank,
+            "heads": h, "reference": "float32 softmax attention in torch on the GPU",
+            "tolerance": {"max_abs": 2e-2, "mean_abs": 2e-3},
+            "pass": bool(mx <= 2e-2 and mean <= 2e-3)}
+
+
 def kernel_case(name: str, dev):
     """Named single-kernel cases (profiling and secondary measurements).
 
@@ -576,7 +613,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # attention-kernel time per layer (all pipelined slices of a step)
     kern_avg = max_over_ranks(sum(kernel_ms) / args.steps) if kernel_ms else float("nan")
     status = _lib.device_status()
-    del out
+    # the timed output's values: sampled rows against a float32 reference
+    parity = parity_sample(out, q, k, v, world, dev)
 
     total_flops = flops(B, H, S_GLOBAL, S_GLOBAL, D)
     value = total_flops / (ms / 1e3) / 1e12
@@ -616,6 +654,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     e2e_value = total_flops / (e2e_ms / 1e3) / 1e12
+    # the host-buffer path computes the same output bits as the device path
+    same = torch.tensor([1.0 if torch.equal(hout, out.cpu()) else 0.0], device=dev)
+    if world > 1:
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    parity["e2e_output_equals_device"] = bool(same.item() == 1.0)
+    del out
     elem = 2
     h2d = 3 * B * s_loc * H * D * elem
     d2h = B * s_loc * H * D * elem
@@ -695,6 +739,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "gpu_launches": gpu_launches,
         "clocks": clocks,
         "device_status": status,
+        "parity": parity,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

@@ -68,7 +68,8 @@ typedef struct vx_attn_args {
   int64_t o_stride[3];
   int32_t batch, seq_q, seq_k, heads_q, heads_kv, head_dim;
   float scale;             /* softmax scale, > 0 */
-  const int32_t* kv_len;   /* optional device int32[B]; NULL = all seq_k keys valid */
+  const int32_t* kv_len;   /* optional device int32[B]; NULL = all seq_k keys valid;
+                              kv_len[b] <= 0 writes zero rows (and lse -inf) for item b */
   float* lse;              /* optional device fp32 (B, Hq, Sq): natural-log sum-exp */
   int32_t schedule;        /* VX_SCHED_STATIC (default) or VX_SCHED_DYNAMIC */
 } vx_attn_args;
@@ -252,7 +253,11 @@ int vx_gated_residual(float* x, const void* y, const float* gate, int64_t rows, 
  * cycles. The wait gives up, raises the CTA's abort flag and records status
  * bit 16 in the device status word; returns VX_ETIMEOUT with *status_out set
  * to the status word (VX_ECUDA if the wait did not behave as specified). The
- * context stays usable; clear the word with vx_device_status(.., 1). */
+ * context stays usable; clear the word with vx_device_status(.., 1).
+ * All calls on a device share one file-scope 2-int __device__ array for the
+ * wait's report: calls that overlap (e.g. from two host threads) race on it
+ * and must be serialised by the caller. *status_out is the whole status word,
+ * so it may also carry bits that other kernels running meanwhile set. */
 int vx_selftest_wait_timeout(int64_t limit_cycles, int* status_out);
 
 #ifdef __cplusplus

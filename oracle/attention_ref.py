@@ -61,14 +61,19 @@ def seeded_qkv(shape, seed: int, head_scale_range=None, n=3):
     return out
 
 
-def sdpa(q, k, v, scale=None, kv_len=None, round_probs=False, q_rows=None, chunk=512):
+def sdpa(q, k, v, scale=None, kv_len=None, round_probs=False, q_rows=None, chunk=512,
+         key_mask=None, key_bias=None):
     """Non-causal attention over BSHD float32 arrays (values bf16-exact).
 
     q: (B, Sq, H, D); k, v: (B, Sk, Hkv, D), H % Hkv == 0 (head h reads kv
     head h // (H // Hkv)). kv_len: optional per-batch count of visible keys
     (keys >= kv_len[b] are masked, the SegmentIds padding rule of
     attention.py:272-278). q_rows: optional index array of query rows to
-    evaluate (returns (B, len(q_rows), H, D)). Returns float32.
+    evaluate (returns (B, len(q_rows), H, D)). key_mask (B, Sk) bool /
+    key_bias (B, Sk) float: jax.nn.dot_product_attention's mask and additive
+    bias restricted to keys -- masked logits become -0.7 * float32 max (so a
+    row with no visible key has uniform weights), the bias is added to the
+    scaled logits (a row of -inf gives NaN). Returns float32.
     """
     q = np.asarray(q, np.float32)
     k = np.asarray(k, np.float32)
@@ -90,7 +95,13 @@ def sdpa(q, k, v, scale=None, kv_len=None, round_probs=False, q_rows=None, chunk
             for r0 in range(0, len(rows), chunk):
                 rr = rows[r0:r0 + chunk]
                 logits = (q[b, rr, h, :] @ kh.T) * np.float32(scale)   # f32
-                logits -= logits.max(axis=1, keepdims=True)
+                if key_bias is not None:
+                    logits = logits + np.asarray(key_bias, np.float32)[b, None, :nk]
+                if key_mask is not None:
+                    logits = np.where(np.asarray(key_mask)[b, None, :nk], logits,
+                                      np.float32(-0.7 * np.finfo(np.float32).max))
+                with np.errstate(invalid="ignore"):
+                    logits -= logits.max(axis=1, keepdims=True)
                 p = np.exp(logits)
                 p /= p.sum(axis=1, keepdims=True)
                 if round_probs:

@@ -71,3 +71,59 @@ def norm_rope(x, weight, cos, sin, heads, eps=1e-6):
     B, S, dim = x.shape
     y = rms_norm(x, weight, eps).reshape(B, S, heads, dim // heads)
     return apply_rope3d(y, cos, sin)
+
+
+# ---------------------------------------------------------------- LTX-2.5
+def ltx_default_rope_split(head_dim):
+    """`_default_rope_dim_split` (src/vidax/models/ltx2_5/diffusion_vae.py:96-103)."""
+    d_t = (head_dim // 4) // 2 * 2
+    d_hw = (head_dim - d_t) // 2
+    if d_hw % 2 != 0:
+        d_t -= 2
+        d_hw = (head_dim - d_t) // 2
+    return d_t, d_hw, d_hw
+
+
+def ltx_inv_freqs(dim, base=10000.0):
+    """`_rope_inv_freqs` (diffusion_vae.py:106-109): float64 formula, float32 result."""
+    return (1.0 / np.power(float(base), np.arange(0, dim, 2, dtype=np.float64) / dim)).astype(np.float32)
+
+
+def ltx_abs_rope(x, split=None, base=10000.0):
+    """`_apply_abs_rope` (diffusion_vae.py:112-150) on x (B, T, H, W, NH, HD)
+    float32 holding bf16 values: head_dim split into (d_t, d_h, d_w) chunks,
+    chunk a's interleaved pairs rotated by float32(position_a) * inv_freq in
+    float32, (e, o) -> (e c - o s, e s + o c), the result rounded to bf16."""
+    x = np.asarray(x, np.float32)
+    HD = x.shape[-1]
+    split = tuple(split or ltx_default_rope_split(HD))
+    outs, off = [], 0
+    for axis, d in zip((1, 2, 3), split):
+        xc = x[..., off:off + d]
+        off += d
+        pairs = xc.reshape(xc.shape[:-1] + (d // 2, 2))
+        xe, xo = pairs[..., 0], pairs[..., 1]
+        pos = np.arange(x.shape[axis], dtype=np.float32)
+        ang = pos[:, None] * ltx_inv_freqs(d, base)[None, :]
+        bshape = [1] * xc.ndim
+        bshape[axis] = pos.shape[0]
+        bshape[-1] = d // 2
+        c = np.cos(ang).astype(np.float32).reshape(bshape)
+        s = np.sin(ang).astype(np.float32).reshape(bshape)
+        re = xe * c - xo * s
+        ro = xe * s + xo * c
+        outs.append(np.stack([re, ro], axis=-1).reshape(xc.shape))
+    return to_bf16(np.concatenate(outs, axis=-1))
+
+
+def ltx_na_prologue(q, k, wq, wk, eps=1e-6, split=None, base=10000.0):
+    """The steps of NeighborhoodAttention3D.__call__ between the projections
+    and the NA primitive (diffusion_vae.py:263-275): per-head RMSNorm of q and
+    k, q * head_dim^-0.5 in bf16 (the scalar rounded to bf16, JAX's weak
+    typing), absolute RoPE on both. Returns (q, k) float32 holding bf16."""
+    HD = np.asarray(q).shape[-1]
+    qn = rms_norm(q, wq, eps)
+    kn = rms_norm(k, wk, eps)
+    c = np.float32(to_bf16(np.float32(HD ** -0.5)))
+    qn = to_bf16(qn * c)
+    return ltx_abs_rope(qn, split, base), ltx_abs_rope(kn, split, base)

@@ -16,7 +16,11 @@ in a namespace where `jax` / `jnp` are a small numpy shim:
   `apply_rope3d` (lines 33-111);
 * src/vidax/core/attention.py: `RMSNorm.__call__` (lines 149-162), run as a
   plain function on a stand-in module object;
-* src/vidax/core/rope3d.py: `sinusoidal_embedding_1d` (lines 15-30).
+* src/vidax/core/rope3d.py: `sinusoidal_embedding_1d` (lines 15-30);
+* src/vidax/models/ltx2_5/diffusion_vae.py: `_default_rope_dim_split`,
+  `_rope_inv_freqs`, `_apply_abs_rope_axis`, `_apply_abs_rope` (lines
+  96-150), and `NeighborhoodAttention3D.__call__` (lines 252-284) with its
+  Dense layers replaced by given projections.
 
 The shim restates the third-party jax primitives the code calls: `jnp.take`,
 `jnp.moveaxis`, `jnp.einsum` (bf16 operands, f32 accumulation, result in the
@@ -243,6 +247,14 @@ def gen_attention():
     out["keypad_len"] = lens
     out["keypad_o_bias"] = ns["dot_product_attention"](q, k, v, bias=bias).astype(np.float32)
     out["keypad_o_mask"] = ns["dot_product_attention"](q, k, v, mask=valid[:, None, None, :]).astype(np.float32)
+    # a batch item with no visible key at all (every key masked / -inf)
+    lens0 = np.array([41, 0], np.int32)
+    valid0 = np.arange(41)[None, :] < lens0[:, None]
+    bias0 = np.where(valid0, 0.0, -np.inf).astype(np.float32)[:, None, None, :]
+    out["keypad0_len"] = lens0
+    with np.errstate(invalid="ignore"):
+        out["keypad0_o_bias"] = ns["dot_product_attention"](q, k, v, bias=bias0).astype(np.float32)
+    out["keypad0_o_mask"] = ns["dot_product_attention"](q, k, v, mask=valid0[:, None, None, :]).astype(np.float32)
     # Ulysses over P emulated devices, each holding its chunk_by_rank share
     for P, (B, S, H, D) in ((2, (1, 16, 4, 8)), (4, (2, 24, 8, 8)), (8, (1, 256, 8, 128))):
         coll = _Collective(P)
@@ -264,13 +276,18 @@ def gen_attention():
         out[f"sp{P}_o"] = np.stack([np.asarray(r).astype(np.float32) for r in results])
     # joint [text; visual] Ulysses (CogVideoX layout): text replicated, visual chunked
     # (the head_dim-128 case is the size the sm_100a kernel takes)
-    for tag, P, (B, T, S, H, D) in (("joint2", 2, (1, 5, 16, 4, 8)), ("joint4", 4, (2, 7, 24, 8, 8)),
-                                    ("joint2d128", 2, (1, 13, 80, 4, 128))):
+    # (joint4d128 / joint2d64: the kernel's head dims at 4 and 2 ranks, distinct seeds)
+    for tag, P, (B, T, S, H, D), seed0 in (
+            ("joint2", 2, (1, 5, 16, 4, 8), None), ("joint4", 4, (2, 7, 24, 8, 8), None),
+            ("joint2d128", 2, (1, 13, 80, 4, 128), None),
+            ("joint4d128", 4, (2, 7, 96, 8, 128), 230), ("joint2d64", 2, (1, 11, 64, 4, 64), 240)):
         coll = _Collective(P)
         ns_p = load_functions("src/vidax/core/attention.py",
                               names + ["sequence_parallel_joint_self_attention"],
                               make_namespace(coll))
-        qg, kg, vg = (seeded((B, T + S, H, D), 110 + P + i + (D > 8) * 7) for i in range(3))
+        if seed0 is None:
+            seed0 = 110 + P + (D > 8) * 7
+        qg, kg, vg = (seeded((B, T + S, H, D), seed0 + i) for i in range(3))
         results = [None] * P
         S_loc = S // P
 
@@ -372,6 +389,135 @@ def gen_sinusoid():
             "sinusoid_emb": np.asarray(ns["sinusoidal_embedding_1d"](256, t), np.float32)}
 
 
+def _ltx_namespace():
+    """Namespace holding diffusion_vae.py's abs-RoPE helpers and the NA
+    primitive, run under the numpy shim (jnp.cos / sin in float32)."""
+    ns = make_namespace()
+    jnp = ns["jnp"]
+    jnp.cos = np.cos
+    jnp.sin = np.sin
+    jnp.stack = np.stack
+    jnp.mean = np.mean
+    jnp.square = np.square
+    ns["math"] = __import__("math")
+    load_functions("src/vidax/models/ltx2_5/diffusion_vae.py",
+                   ["_default_rope_dim_split", "_rope_inv_freqs", "_apply_abs_rope_axis",
+                    "_apply_abs_rope", "_window_start", "_gather_window",
+                    "neighborhood_attention_3d"], ns)
+    return ns
+
+
+def gen_ltx_rope():
+    """LTX-2.5's absolute split RoPE (diffusion_vae.py:96-150): the default
+    split, the inverse frequencies, and `_apply_abs_rope` on small grids at
+    head_dim 64 (the checkpoint's) and 128; also each axis's float32 angle
+    tables cos / sin(position * inv_freq), the product's table entries."""
+    ns = _ltx_namespace()
+    out = {}
+    for i, (t, h, w, hd, split) in enumerate([(3, 4, 5, 64, None), (2, 3, 6, 128, None),
+                                             (4, 2, 3, 64, (8, 28, 28))]):
+        split = tuple(int(x) for x in (split or ns["_default_rope_dim_split"](hd)))
+        invs = [np.asarray(ns["_rope_inv_freqs"](d, 10000.0), np.float32) for d in split]
+        pos = [np.arange(n, dtype=np.float32) for n in (t, h, w)]
+        x = seeded((1, t, h, w, 3, hd), 250 + i)
+        y = ns["_apply_abs_rope"](x, split, tuple(invs), tuple(pos))
+        assert y.dtype == BF16 and y.shape == x.shape
+        out[f"ltxrope{i}_grid"] = np.array([t, h, w, hd], np.int32)
+        out[f"ltxrope{i}_split"] = np.array(split, np.int32)
+        for a, (p_a, inv) in enumerate(zip(pos, invs)):
+            ang = p_a[:, None] * inv[None, :]
+            out[f"ltxrope{i}_cos{a}"] = np.cos(ang).astype(np.float32)
+            out[f"ltxrope{i}_sin{a}"] = np.sin(ang).astype(np.float32)
+        out[f"ltxrope{i}_x"] = x.astype(np.float32)
+        out[f"ltxrope{i}_y"] = y.astype(np.float32)
+    return out
+
+
+class _WeakScalarBF16(np.ndarray):
+    """A bf16 array whose product with a Python scalar follows JAX's weak
+    typing: the scalar takes the array's dtype (bf16) and the result stays
+    bf16, bf16(f32(x) * f32(bf16(c))). numpy with ml_dtypes would promote to
+    float32 instead. Any other operation returns a plain ndarray."""
+
+    def __array_ufunc__(self, ufunc, method, *inputs, **kw):
+        plain = [np.asarray(x) if isinstance(x, _WeakScalarBF16) else x for x in inputs]
+        if (ufunc is np.multiply and method == "__call__" and len(plain) == 2 and not kw
+                and isinstance(plain[1], (float, int)) and plain[0].dtype == BF16):
+            c = np.float32(np.asarray(plain[1], np.float32).astype(BF16))
+            return (plain[0].astype(np.float32) * c).astype(BF16)
+        return getattr(ufunc, method)(*plain, **kw)
+
+
+def gen_ltx_na_block():
+    """The NA caller contract: `NeighborhoodAttention3D.__call__`
+    (diffusion_vae.py:252-284) run as a plain function whose `to_q` / `to_k`
+    / `to_v` Dense layers return given projections and whose `to_out` is the
+    identity, so the reference's own per-head RMSNorm (attention.py:149-162),
+    bf16 q scaling (:265), absolute RoPE (:267-275) and NA call (:277) run on
+    them. Head_dim 64 (the checkpoint's) and 128."""
+    ns = _ltx_namespace()
+    ns["jax"].lax.rsqrt = lambda v: (np.float32(1.0) / np.sqrt(v)).astype(np.float32)
+    rms_ns = make_namespace()
+    rms_ns["jnp"].mean = np.mean
+    rms_ns["jnp"].square = np.square
+    rms_ns["jax"].lax.rsqrt = ns["jax"].lax.rsqrt
+    rms_ns["nn"] = types.SimpleNamespace(initializers=types.SimpleNamespace(ones=None))
+    rms_call = load_method("src/vidax/core/attention.py", "RMSNorm", "__call__", rms_ns)
+    out = {}
+    cases = [((1, 3, 4, 6, 2, 64), (3, 3, 5)), ((1, 2, 5, 7, 2, 64), (3, 5, 5)),
+             ((1, 3, 4, 5, 1, 128), (3, 3, 3))]
+    for i, (shape, kernel) in enumerate(cases):
+        B, T, H, W, NH, HD = shape
+        proj = {n: seeded(shape, 260 + 3 * i + j, scale=2.0) for j, n in enumerate(("to_q", "to_k", "to_v"))}
+        rng = np.random.Generator(np.random.PCG64(270 + i))
+        weights = {n: (1.0 + 0.25 * rng.standard_normal(HD)).astype(np.float32)
+                   for n in ("q_norm", "k_norm")}
+
+        class Dense:
+            def __init__(self, features, name):
+                self.name = name
+
+            def __call__(self, x):
+                if self.name == "to_out":
+                    return x
+                return proj[self.name].reshape(x.shape[:4] + (NH * HD,))
+
+        def rmsnorm(dim, eps=1e-6, name=None):
+            module = types.SimpleNamespace(dim=dim, eps=eps,
+                                           param=lambda pname, init, shp: weights[name])
+            return lambda x: np.asarray(rms_call(module, x)).view(_WeakScalarBF16)
+
+        ns["nn"] = types.SimpleNamespace(Dense=Dense)
+        ns["RMSNorm"] = rmsnorm
+        seen = {}
+        na_fn = ns.get("_na_primitive", ns["neighborhood_attention_3d"])
+        ns["_na_primitive"] = na_fn
+
+        def recording_na(q, k, v, kernel_size, na_fn=na_fn, seen=seen):
+            # the primitive's inputs: q / k after norm, scale and RoPE
+            seen["q"], seen["k"] = q, k
+            return na_fn(q, k, v, kernel_size)
+
+        ns["neighborhood_attention_3d"] = recording_na
+        call = load_method("src/vidax/models/ltx2_5/diffusion_vae.py", "NeighborhoodAttention3D",
+                           "__call__", ns)
+        module = types.SimpleNamespace(dim=NH * HD, kernel_size=kernel, head_dim=HD,
+                                       rope_dim_split=None, rope_base=10000.0, eps=1e-6)
+        x = np.zeros((B, T, H, W, NH * HD), BF16)
+        o = call(module, x)
+        assert o.dtype == BF16
+        for n, tag in (("to_q", "q"), ("to_k", "k"), ("to_v", "v")):
+            out[f"ltxna{i}_{tag}"] = proj[n].astype(np.float32)
+        out[f"ltxna{i}_wq"] = weights["q_norm"]
+        out[f"ltxna{i}_wk"] = weights["k_norm"]
+        out[f"ltxna{i}_kernel"] = np.array(kernel, np.int32)
+        out[f"ltxna{i}_o"] = np.asarray(o, np.float32).reshape(shape)
+        assert seen["q"].dtype == BF16 and seen["k"].dtype == BF16
+        out[f"ltxna{i}_qr"] = seen["q"].astype(np.float32)
+        out[f"ltxna{i}_kr"] = seen["k"].astype(np.float32)
+    return out
+
+
 def main():
     if not REF or not os.path.isdir(REF):
         sys.exit("usage: make_golden.py <path-to-vidax-checkout>")
@@ -383,7 +529,11 @@ def main():
     ro.update(gen_rmsnorm())
     ro.update(gen_sinusoid())
     np.savez_compressed(os.path.join(OUT_DIR, "rope_reference.npz"), **ro)
-    for f in ("na3d_reference.npz", "attention_reference.npz", "rope_reference.npz"):
+    ltx = gen_ltx_rope()
+    ltx.update(gen_ltx_na_block())
+    np.savez_compressed(os.path.join(OUT_DIR, "ltx_reference.npz"), **ltx)
+    for f in ("na3d_reference.npz", "attention_reference.npz", "rope_reference.npz",
+              "ltx_reference.npz"):
         print(f, os.path.getsize(os.path.join(OUT_DIR, f)), "bytes")
 
 

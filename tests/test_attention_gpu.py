@@ -87,6 +87,29 @@ def test_cfg2_head_scaled_sampled_rows():
 
 
 @pytest.mark.gpu
+def test_cfg3_bench_shape_sampled_rows_every_head():
+    """BASELINE config 3 at the bench's own shape, (1, 75600, 40, 128), N(0,1)
+    seed 3: the headline workload. Seeded query rows (both ends of the
+    sequence, including the 80-row partial last block, and 120 random rows),
+    every one of the 40 heads (about 200 rows x 40 heads), against the oracle."""
+    import vidax_b200 as vx
+    S = 75600
+    q, k, v = seeded_qkv((1, S, 40, 128), 3)
+    out = vx.dot_product_attention(_dev(q), _dev(k), _dev(v))
+    torch.cuda.synchronize()
+    assert _status_clean()
+    rows = np.unique(np.concatenate([
+        np.arange(0, 4), np.arange(S - 76, S),
+        np.random.default_rng(3).integers(0, S, 120)]))
+    got = _host(out[:, torch.from_numpy(rows).cuda()])
+    del out
+    ref = sdpa(q, k, v, q_rows=rows)
+    assert np.isfinite(got).all()
+    mx, mean = compare(got, ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
 def test_kv_len_padding_mask():
     """Keys at index >= kv_len[b] are invisible (SegmentIds padding rule)."""
     import vidax_b200 as vx

@@ -65,6 +65,28 @@ def test_key_padding_vs_reference_code():
 
 
 @pytest.mark.gpu
+def test_fully_masked_key_row_vs_reference_code():
+    """A batch item with no visible key (valid lengths 41 and 0): the mask
+    form gives the reference's mean of v over all keys, the -inf bias form its
+    NaN rows; device and host inputs alike."""
+    import vidax_b200 as vx
+    g = np.load(os.path.join(GOLDEN, "attention_reference.npz"))
+    q, k, v = _dev(g["keypad_q"]), _dev(g["keypad_k"]), _dev(g["keypad_v"])
+    lens = torch.from_numpy(g["keypad0_len"]).long()
+    valid = torch.arange(k.shape[1])[None, :] < lens[:, None]
+    bias = torch.zeros(valid.shape).masked_fill(~valid, float("-inf"))[:, None, None, :]
+    for host in (False, True):
+        args = [t.cpu().pin_memory() for t in (q, k, v)] if host else [q, k, v]
+        o_mask = vx.dot_product_attention(*args, mask=valid[:, None, None, :]).float().cpu().numpy()
+        mx, mean = compare(o_mask, g["keypad0_o_mask"])
+        assert mx <= MAX_ABS and mean <= MEAN_ABS, (host, mx, mean)
+        o_bias = vx.dot_product_attention(*args, bias=bias).float().cpu().numpy()
+        assert np.isnan(o_bias[1]).all() and not np.isnan(o_bias[0]).any()
+        mx, mean = compare(o_bias[0], g["keypad0_o_bias"][0])
+        assert mx <= MAX_ABS and mean <= MEAN_ABS, (host, mx, mean)
+
+
+@pytest.mark.gpu
 def test_ulysses_kernels_vs_reference_code():
     """P=8 Ulysses (1, 256, 8, 128): pack -> (chunk copies standing in for the
     NCCL all-to-all) -> attention -> unpack, per emulated rank, against the

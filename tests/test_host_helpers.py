@@ -145,3 +145,26 @@ def test_bench_host_cpu_record():
     import bench
     h = bench.host_cpu()
     assert set(h) == {"cpu_model", "logical_cpus"} and h["logical_cpus"] >= 1
+
+
+def test_fully_masked_rows_modes():
+    """Which batch items have no visible key, and what the reference gives
+    them: mask form -> mean of v, -inf bias -> NaN, one finite padding value
+    -> mean; unequal finite padding values are refused."""
+    import pytest
+    import torch
+    from vidax_b200.attention import _fully_masked_rows, _key_lengths_from_bias, _key_lengths_from_mask
+    B, Sk = 3, 5
+    valid = torch.tensor([[1, 1, 0, 0, 0], [0, 0, 0, 0, 0], [1, 1, 1, 1, 1]], dtype=torch.bool)
+    lens = _key_lengths_from_mask(valid[:, None, None, :], B, Sk)
+    assert lens.tolist() == [2, 0, 5]
+    assert _fully_masked_rows(None, valid[:, None, None, :], lens, B, Sk) == [(1, "mean")]
+    bias = torch.where(valid, 0.0, float("-inf"))[:, None, None, :]
+    lens = _key_lengths_from_bias(bias, B, Sk)
+    assert _fully_masked_rows(bias, None, lens, B, Sk) == [(1, "nan")]
+    bias2 = torch.where(valid, 0.0, -1e9)[:, None, None, :]
+    assert _fully_masked_rows(bias2, None, _key_lengths_from_bias(bias2, B, Sk), B, Sk) == [(1, "mean")]
+    bias3 = bias2.clone()
+    bias3[1, 0, 0, 0] = -2e9
+    with pytest.raises(NotImplementedError):
+        _fully_masked_rows(bias3, None, _key_lengths_from_bias(bias3, B, Sk), B, Sk)

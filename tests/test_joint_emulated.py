@@ -3,79 +3,23 @@ as P emulated ranks in one process, against the reference's own per-rank
 outputs (tests/golden, written by make_golden.py from vidax's function).
 
 Each rank is a thread; `torch.distributed` inside vidax_b200.ulysses is
-replaced by an in-process stand-in whose all_to_all_single /
-all_gather_into_tensor exchange the ranks' tensors through shared memory
-behind a barrier (with a timeout: a failing rank breaks the barrier instead
-of hanging the others). The product's own orchestration -- text slicing,
+replaced by the in-process stand-in of tests/emulated_ranks.py. The product's own orchestration -- text slicing,
 packing, exchange, joint attention, reverse exchange, text all-gather --
 runs unchanged, with the kernels replaced by float32 torch equivalents
-(this pins the orchestration; the kernels themselves are pinned by
-tests/test_golden_gpu.py and the 2-GPU NCCL test). `_run_joint` also takes
-the CUDA device and the real kernels. Tolerance: max-abs 2e-2, mean-abs
-2e-3."""
+(this pins the orchestration on any host), and on a GPU with the real
+kernels (pack, attention, unpack) at the head dims the kernel takes (128,
+64). Tolerance: max-abs 2e-2, mean-abs 2e-3."""
 import os
-import threading
 
 import numpy as np
 import pytest
 import torch
 
+from emulated_ranks import RankGroup, run_ranks
 from oracle.attention_ref import compare
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
-
-
-class _Done:
-    def wait(self):
-        return True
-
-
-class _RankGroup:
-    """The collectives the joint path calls, for P threads of one process."""
-
-    def __init__(self, P: int):
-        self.P = P
-        self.barrier = threading.Barrier(P, timeout=120)
-        self.local = threading.local()
-        self.slots = [None] * P
-
-    def get_world_size(self, group=None):
-        return self.P
-
-    def get_rank(self, group=None):
-        return self.local.rank
-
-    @staticmethod
-    def _settle(t):
-        if t.is_cuda:
-            torch.cuda.synchronize(t.device)
-
-    def _publish(self, t):
-        self._settle(t)
-        self.slots[self.local.rank] = t
-        self.barrier.wait()
-
-    def _done(self, t):
-        self._settle(t)
-        self.barrier.wait()  # every rank has read the slots
-
-    def all_to_all_single(self, output, input, output_split_sizes=None, input_split_sizes=None,
-                          group=None, async_op=False):
-        assert output_split_sizes is None and input_split_sizes is None
-        self._publish(input)
-        r = self.local.rank
-        output.view(self.P, -1).copy_(
-            torch.stack([self.slots[s].reshape(self.P, -1)[r] for s in range(self.P)]))
-        self._done(output)
-        return _Done() if async_op else None
-
-    def all_gather_into_tensor(self, output, input, group=None, async_op=False):
-        self._publish(input)
-        output.view(self.P, -1).copy_(
-            torch.stack([self.slots[s].reshape(-1) for s in range(self.P)]))
-        self._done(output)
-        return _Done() if async_op else None
 
 
 def _cpu_attention(q, k, v, scale, **_):
@@ -118,36 +62,25 @@ def _run_joint(tag, monkeypatch, device, dtype, cpu_kernels):
     ref = g[f"{tag}_o"]
     P = ref.shape[0]
     S_loc = (qg.shape[1] - T) // P
-    fake = _RankGroup(P)
+    fake = RankGroup(P)
     monkeypatch.setattr(ulysses, "dist", fake)
     if cpu_kernels:
         monkeypatch.setattr(ulysses, "flash_attention", _cpu_attention)
         monkeypatch.setattr(ulysses, "pack_heads", _cpu_pack)
         monkeypatch.setattr(ulysses, "unpack_heads", _cpu_unpack)
     vx.register_axis("sp_emulated", None)
-    results, errors = [None] * P, []
 
     def rank(r):
-        try:
-            fake.local.rank = r
-            loc = [torch.from_numpy(np.ascontiguousarray(np.concatenate(
-                [x[:, :T], x[:, T + r * S_loc:T + (r + 1) * S_loc]], axis=1))).to(device, dtype)
-                for x in (qg, kg, vg)]
-            o = vx.sequence_parallel_joint_self_attention(*loc, T, "sp_emulated")
-            results[r] = o.float().cpu().numpy()
-        except BaseException as e:  # noqa: BLE001 -- reported below
-            errors.append(f"rank {r}: {type(e).__name__}: {e}")
-            fake.barrier.abort()
+        loc = [torch.from_numpy(np.ascontiguousarray(np.concatenate(
+            [x[:, :T], x[:, T + r * S_loc:T + (r + 1) * S_loc]], axis=1))).to(device, dtype)
+            for x in (qg, kg, vg)]
+        o = vx.sequence_parallel_joint_self_attention(*loc, T, "sp_emulated")
+        return o.float().cpu().numpy()
 
-    threads = [threading.Thread(target=rank, args=(r,)) for r in range(P)]
     try:
-        for t in threads:
-            t.start()
-        for t in threads:
-            t.join(timeout=300)
+        results = run_ranks(P, fake, rank)
     finally:
         vx.unregister_axis("sp_emulated")
-    assert not errors, errors
     for r in range(P):
         mx, mean = compare(results[r], ref[r])
         assert mx <= MAX_ABS and mean <= MEAN_ABS, (tag, r, mx, mean)
@@ -158,3 +91,14 @@ def test_joint_orchestration_matches_reference_code(tag, monkeypatch):
     """CPU: the product's joint Ulysses orchestration with float32 torch
     attention / packing in place of the kernels."""
     _run_joint(tag, monkeypatch, "cpu", torch.float32, cpu_kernels=True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tag", ["joint2d128", "joint4d128", "joint2d64"])
+def test_joint_on_cuda_kernels_matches_reference_code(tag, monkeypatch):
+    """GPU: the same orchestration with the CUDA pack / attention / unpack
+    kernels, bf16, against the reference's per-rank outputs (P = 2 and 4,
+    head_dim 128 and 64)."""
+    from vidax_b200 import _lib
+    _run_joint(tag, monkeypatch, "cuda", torch.bfloat16, cpu_kernels=False)
+    assert _lib.device_status(clear=True) == 0

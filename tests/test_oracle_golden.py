@@ -163,3 +163,85 @@ def test_key_padding_matches_reference_code(attn_gold):
     got = to_bf16(sdpa(q, k, v, kv_len=lens, round_probs=True))
     _assert_bf16_close(got, attn_gold["keypad_o_bias"])
     _assert_bf16_close(got, attn_gold["keypad_o_mask"])
+
+
+@pytest.mark.parametrize("P,tag", [(4, "joint4d128"), (2, "joint2d64")])
+def test_joint_ulysses_kernel_sized_fixtures(attn_gold, P, tag):
+    """The head_dim-128 / 64 joint fixtures (the sizes the CUDA kernel takes)
+    against the oracle, as for the small ones."""
+    qg, kg, vg = (attn_gold[f"{tag}_{n}"] for n in "qkv")
+    T = int(attn_gold[f"{tag}_text_len"][0])
+    ref = attn_gold[f"{tag}_o"]
+    full = to_bf16(sdpa(qg, kg, vg, round_probs=True))
+    S_loc = (qg.shape[1] - T) // P
+    for r in range(P):
+        want = np.concatenate([full[:, :T], full[:, T + r * S_loc:T + (r + 1) * S_loc]], axis=1)
+        _assert_bf16_close(want, ref[r])
+
+
+@pytest.fixture(scope="module")
+def ltx_gold():
+    return np.load(os.path.join(GOLDEN, "ltx_reference.npz"))
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_ltx_abs_rope_oracle_matches_reference_code(ltx_gold, i):
+    """LTX-2.5's absolute split RoPE (diffusion_vae.py:96-150): the oracle's
+    restatement is bit-exact against the reference's own `_apply_abs_rope`."""
+    from oracle.rope_norm_ref import ltx_abs_rope, ltx_default_rope_split
+    split = tuple(int(x) for x in ltx_gold[f"ltxrope{i}_split"])
+    hd = int(ltx_gold[f"ltxrope{i}_grid"][3])
+    if i < 2:
+        assert ltx_default_rope_split(hd) == split
+    y = ltx_abs_rope(ltx_gold[f"ltxrope{i}_x"], split)
+    assert np.array_equal(y, ltx_gold[f"ltxrope{i}_y"])
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_ltx_rope_tables_match_reference_code(ltx_gold, i):
+    """The product's table builder (host numpy, no device needed): every
+    token's pair p holds cos / sin of its axis's float32 angle exactly as the
+    reference computes it."""
+    from vidax_b200.prologue import ltx_default_rope_split, ltx_rope_freqs
+    t, h, w, hd = (int(x) for x in ltx_gold[f"ltxrope{i}_grid"])
+    split = tuple(int(x) for x in ltx_gold[f"ltxrope{i}_split"])
+    if i < 2:
+        assert ltx_default_rope_split(hd) == split
+    cos, sin = (x.numpy().reshape(t, h, w, hd // 2) for x in ltx_rope_freqs(t, h, w, hd, split))
+    d0, d1 = split[0] // 2, (split[0] + split[1]) // 2
+    for k, tab in (("cos", cos), ("sin", sin)):
+        ref0, ref1, ref2 = (ltx_gold[f"ltxrope{i}_{k}{a}"] for a in range(3))
+        assert np.array_equal(tab[..., :d0], np.broadcast_to(ref0[:, None, None, :], (t, h, w, d0)))
+        assert np.array_equal(tab[..., d0:d1], np.broadcast_to(ref1[None, :, None, :], (t, h, w, d1 - d0)))
+        assert np.array_equal(tab[..., d1:], np.broadcast_to(ref2[None, None, :, :], (t, h, w, hd // 2 - d1)))
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_ltx_na_block_oracle_matches_reference_code(ltx_gold, i):
+    """NeighborhoodAttention3D.__call__ between its projections (per-head
+    RMSNorm, bf16 q scale, abs RoPE, NA): the oracle's q / k after the
+    prologue are bit-exact, its output within the bf16 rounding spread."""
+    from oracle.rope_norm_ref import ltx_na_prologue
+    q, k, v = (ltx_gold[f"ltxna{i}_{n}"] for n in "qkv")
+    qr, kr = ltx_na_prologue(q, k, ltx_gold[f"ltxna{i}_wq"], ltx_gold[f"ltxna{i}_wk"])
+    assert np.array_equal(qr, ltx_gold[f"ltxna{i}_qr"])
+    assert np.array_equal(kr, ltx_gold[f"ltxna{i}_kr"])
+    kernel = tuple(int(x) for x in ltx_gold[f"ltxna{i}_kernel"])
+    got = to_bf16(na3d(qr, kr, v, kernel, round_logits=True, round_probs=True))
+    _assert_bf16_close(got, ltx_gold[f"ltxna{i}_o"])
+
+
+def test_fully_masked_key_row_matches_reference_code(attn_gold):
+    """A batch item with no visible key: jax.nn's mask form gives the mean of
+    v over all keys (uniform weights), its -inf bias form gives NaN."""
+    q, k, v = attn_gold["keypad_q"], attn_gold["keypad_k"], attn_gold["keypad_v"]
+    lens = attn_gold["keypad0_len"]
+    valid = np.arange(k.shape[1])[None, :] < lens[:, None]
+    got = to_bf16(sdpa(q, k, v, key_mask=valid, round_probs=True))
+    _assert_bf16_close(got, attn_gold["keypad0_o_mask"])
+    assert np.isnan(attn_gold["keypad0_o_bias"][1]).all()
+    bias = np.where(valid, 0.0, -np.inf).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        got = to_bf16(sdpa(q, k, v, key_bias=bias, round_probs=True))
+    assert np.isnan(got[1]).all()
+    _assert_bf16_close(got[0], attn_gold["keypad0_o_bias"][0])

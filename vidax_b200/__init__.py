@@ -20,13 +20,20 @@ from .attention import (  # noqa: F401
 )
 from .hostio import attention_from_host  # noqa: F401
 from .neighborhood import (  # noqa: F401
+    ltx_neighborhood_attention,
     na3d_flops,
     neighborhood_attention_3d,
     neighborhood_attention_3d_slab,
 )
 from .na_parallel import neighborhood_attention_3d_sp  # noqa: F401
 from .ulysses_qsplit import sequence_parallel_self_attention_qsplit  # noqa: F401
-from .prologue import attend, norm_rope_pack, rms_norm_rope, rope3d_freqs  # noqa: F401
+from .prologue import (  # noqa: F401
+    attend,
+    ltx_rope_freqs,
+    norm_rope_pack,
+    rms_norm_rope,
+    rope3d_freqs,
+)
 from .ulysses import (  # noqa: F401
     axis_index,
     axis_size,

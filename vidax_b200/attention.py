@@ -139,6 +139,52 @@ def _key_lengths_from_bias(bias: torch.Tensor, B: int, Sk: int) -> torch.Tensor:
     return _key_lengths_from_mask(valid, B, Sk)
 
 
+def _fully_masked_rows(bias: Optional[torch.Tensor], mask: Optional[torch.Tensor],
+                       lens: torch.Tensor, B: int, Sk: int):
+    """Batch items whose every key is masked, and what the reference gives
+    for them (jax.nn.dot_product_attention, attention.py:533): with a boolean
+    mask the masked logits become one large negative number, so the weights
+    are uniform and each output row is the mean of v over all Sk keys
+    ("mean"); with an additive bias of -inf the softmax is 0/0 ("nan"); a
+    row of one finite large negative value is uniform again ("mean").
+    Returns [(b, mode)]."""
+    empty = [int(b) for b in torch.nonzero(lens.cpu() == 0).flatten()]
+    if not empty or Sk == 0:
+        return []
+    if mask is not None:
+        return [(b, "mean") for b in empty]
+    bb = bias
+    while bb.dim() < 4:
+        bb = bb.unsqueeze(0)
+    rows = bb.reshape(bb.shape[0], Sk).expand(B, Sk).float().cpu()
+    out = []
+    for b in empty:
+        r = rows[b]
+        if bool(torch.isneginf(r).all()):
+            out.append((b, "nan"))
+        elif bool((r == r[0]).all()):
+            out.append((b, "mean"))
+        else:
+            raise NotImplementedError(
+                "a fully masked key row with unequal padding-bias values is not supported")
+    return out
+
+
+def _fill_fully_masked(out: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rows, scale: float):
+    """Writes the reference's result for fully masked batch items into `out`
+    (device or host): NaN, or the mean of v over all keys, computed by the
+    attention kernel with a zero query (all logits 0: uniform weights)."""
+    for b, mode in rows:
+        if mode == "nan":
+            out[b].fill_(float("nan"))
+            continue
+        dev = out.device if out.is_cuda else torch.device("cuda", torch.cuda.current_device())
+        kb, vb = k[b:b + 1].to(dev), v[b:b + 1].to(dev)
+        zq = torch.zeros((1, 1, out.shape[2], out.shape[3]), dtype=torch.bfloat16, device=dev)
+        m = flash_attention(zq, kb, vb, scale)
+        out[b].copy_(m[0].expand(out.shape[1], -1, -1))
+
+
 def local_attention(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None,
 ) -> torch.Tensor:
@@ -168,7 +214,10 @@ def dot_product_attention(
     `bias` / `mask` are accepted only in their key-padding forms ((B,1,1,Sk)
     0/-inf bias or boolean valid-prefix mask), which become per-batch key
     lengths for the kernel; dense biases and general masks raise
-    NotImplementedError. `mesh` marks q/k/v as this rank's Megatron head
+    NotImplementedError. A batch item with no visible key gets what the
+    reference gives it: the mean of v over all keys (mask form, or a row of
+    one finite padding value) or NaN (a row of -inf biases); the C ABI's
+    kv_len = 0 itself writes zero rows. `mesh` marks q/k/v as this rank's Megatron head
     shard (`P('dp', None, 'tp', None)`, attention.py:293-318): heads are
     independent, so the local kernel runs with no communication.
     """
@@ -177,19 +226,26 @@ def dot_product_attention(
     head_dim = q.shape[-1]
     sm_scale = head_dim ** -0.5 if scale is None else scale
     kv_len = None
+    empty = []
     if mask is not None and bias is not None:
         raise NotImplementedError("bias and mask together are not supported")
     if mask is not None:
         kv_len = _key_lengths_from_mask(mask, B, Sk)
     elif bias is not None:
         kv_len = _key_lengths_from_bias(bias, B, Sk)
+    if kv_len is not None:
+        empty = _fully_masked_rows(bias, mask, kv_len, B, Sk)
     if q.device.type == "cpu":
         # host tensors: transfers pipelined against the kernel (vidax_b200.hostio)
         from .hostio import attention_from_host
-        return attention_from_host(q, k, v, sm_scale, kv_len=kv_len)
-    if kv_len is not None:
-        kv_len = kv_len.to(device=q.device)  # the mask / bias may live on the host
-    return flash_attention(q, k, v, sm_scale, kv_len=kv_len)
+        out = attention_from_host(q, k, v, sm_scale, kv_len=kv_len)
+    else:
+        if kv_len is not None:
+            kv_len = kv_len.to(device=q.device)  # the mask / bias may live on the host
+        out = flash_attention(q, k, v, sm_scale, kv_len=kv_len)
+    if empty:
+        _fill_fully_masked(out, k, v, empty, sm_scale)
+    return out
 
 
 def chunk_by_rank(x: torch.Tensor, axis: int, sp_size: int, rank: int) -> torch.Tensor:

@@ -153,6 +153,47 @@ def _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, slab):
     return out
 
 
+def bf16_scalar(x: float) -> float:
+    """`x` rounded to bf16 (round to nearest even): what a Python scalar
+    becomes when JAX multiplies it into a bf16 array (weak typing)."""
+    return float(torch.tensor(x, dtype=torch.float32).bfloat16().float())
+
+
+def ltx_neighborhood_attention(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kernel_size: Sequence[int], *,
+    norm_q: torch.Tensor, norm_k: torch.Tensor, eps: float = 1e-6,
+    rope_split: Optional[Sequence[int]] = None, rope_base: float = 10000.0,
+    rope: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+) -> torch.Tensor:
+    """LTX-2.5's neighborhood attention between its projections
+    (`NeighborhoodAttention3D.__call__`, src/vidax/models/ltx2_5/
+    diffusion_vae.py:252-284, from after to_q / to_k / to_v to before
+    to_out): per-head RMSNorm of q and k (weights `norm_q` / `norm_k`,
+    head_dim floats, src/vidax/core/attention.py:149-162), q scaled by
+    head_dim^-0.5 in bf16 (:265; JAX rounds the scalar to bf16 first),
+    LTX's absolute split RoPE on q and k (:267-275, tables from
+    `ltx_rope_freqs` unless `rope` is given), then the NA primitive (:277).
+
+    q, k, v: (B, T, H, W, NH, HD) bf16 projections. The norms, the scale and
+    the rotation of q and k run as one `vx_norm_rope_pack` launch (one HBM
+    read and write of q and k), then one `vx_na3d_fwd` launch. Returns
+    (B, T, H, W, NH, HD) bf16."""
+    from .prologue import ltx_rope_freqs, norm_rope_pack
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check6(name, t)
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError("q, k, v must have the same (B, T, H, W, NH, HD) shape")
+    B, T, H, W, NH, HD = q.shape
+    if rope is None:
+        rope = ltx_rope_freqs(T, H, W, HD, rope_split, rope_base, device=q.device)
+    rows = [t.reshape(B, T * H * W, NH, HD) for t in (q, k)]
+    qr, kr = norm_rope_pack(rows, NH, norm_weights=[norm_q, norm_k], per_head=True, eps=eps,
+                            post_scale=[bf16_scalar(HD ** -0.5), 1.0], rope=rope,
+                            rope_mask=0b11)
+    shape = (B, T, H, W, NH, HD)
+    return neighborhood_attention_3d(qr.view(shape), kr.view(shape), v, kernel_size)
+
+
 def na3d_flops(B: int, T: int, H: int, W: int, NH: int, HD: int, kernel_size) -> float:
     """Algorithmic FLOPs, 4 * queries * |window| * HD * NH (window clamped to the grid)."""
     kt, kh, kw = (min(a, b) for a, b in zip(kernel_size, (T, H, W)))

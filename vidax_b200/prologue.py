@@ -96,6 +96,57 @@ def rope3d_freqs(t: int, h: int, w: int, head_dim: int, theta: float = 10000.0,
     return tab[:, :c], tab[:, c:]
 
 
+def ltx_default_rope_split(head_dim: int) -> Tuple[int, int, int]:
+    """LTX-2.5's split of head_dim into (T, H, W) RoPE chunks
+    (`_default_rope_dim_split`, src/vidax/models/ltx2_5/diffusion_vae.py:
+    96-103): T gets (head_dim // 4) rounded down to even, H and W share the
+    rest equally, and T gives up 2 more when that share would be odd."""
+    d_t = (head_dim // 4) // 2 * 2
+    d_hw = (head_dim - d_t) // 2
+    if d_hw % 2:
+        d_t -= 2
+        d_hw = (head_dim - d_t) // 2
+    return d_t, d_hw, d_hw
+
+
+def ltx_rope_freqs(t: int, h: int, w: int, head_dim: int,
+                   rope_split: Optional[Sequence[int]] = None, base: float = 10000.0,
+                   device=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """LTX-2.5's absolute split RoPE as (cos, sin) tables for a (t, h, w)
+    token grid (`_rope_inv_freqs` / `_apply_abs_rope`, diffusion_vae.py:
+    106-150). head_dim is split into (d_t, d_h, d_w) chunks (default
+    `ltx_default_rope_split`); each chunk rotates its interleaved pairs at
+    its axis's absolute position with inv_freq = 1 / base^(2i / d) (float64,
+    rounded to float32) and angle = float32(position) * inv_freq in float32.
+    Returns (cos, sin), each (t*h*w, head_dim // 2) float32, token-major in
+    (t, h, w) order: pair p < d_t/2 uses the time position, the next d_h/2
+    pairs the row, the last d_w/2 the column -- the interleaved-pair table
+    `norm_rope_pack` applies."""
+    split = tuple(int(x) for x in (rope_split or ltx_default_rope_split(head_dim)))
+    if len(split) != 3 or sum(split) != head_dim or any(d <= 0 or d % 2 for d in split):
+        raise ValueError(f"rope_split {split} must be three positive even sizes summing to "
+                         f"head_dim {head_dim}")
+    c = head_dim // 2
+    per_axis = []
+    for n, d in zip((t, h, w), split):
+        inv = (1.0 / np.power(float(base), np.arange(0, d, 2, dtype=np.float64) / d)).astype(np.float32)
+        ang = np.arange(n, dtype=np.float32)[:, None] * inv[None, :]
+        per_axis.append((np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)))
+    both = np.empty((t * h * w, 2 * c), dtype=np.float32)  # [cos | sin] per token
+    dims = [d // 2 for d in split]
+    for k in range(2):
+        ft, fh, fw = (tab[k] for tab in per_axis)
+        both[:, k * c:(k + 1) * c] = np.concatenate([
+            np.broadcast_to(ft[:, None, None, :], (t, h, w, dims[0])),
+            np.broadcast_to(fh[None, :, None, :], (t, h, w, dims[1])),
+            np.broadcast_to(fw[None, None, :, :], (t, h, w, dims[2])),
+        ], axis=-1).reshape(t * h * w, c)
+    tab = torch.from_numpy(both)
+    if device is not None:
+        tab = tab.to(device)
+    return tab[:, :c], tab[:, c:]
+
+
 # ------------------------------------------------------------------ launch
 
 

@@ -463,10 +463,15 @@ def sequence_parallel_joint_self_attention(
         packed = pack_heads([q[b, text_len:], k[b, text_len:], v[b, text_len:]], P)
         joint = []
         for t_full, t_send in zip((q[b], k[b], v[b]), packed):
-            # [text rows of this head group ; received visual rows (P, S_loc, Hg, D)]
-            buf = torch.zeros((text_len + P * S_loc, Hg, D), dtype=q.dtype, device=q.device)
-            if h1 > h0:
-                buf[:text_len, : h1 - h0].copy_(t_full[:text_len, h0:h1])
+            # [text rows of this head group ; received visual rows (P, S_loc, Hg, D)]:
+            # the exchange writes every visual row, so only the text rows are
+            # filled here (zero heads only past H, when H % P != 0)
+            buf = torch.empty((text_len + P * S_loc, Hg, D), dtype=q.dtype, device=q.device)
+            nvalid = max(h1 - h0, 0)
+            if nvalid > 0:
+                buf[:text_len, :nvalid].copy_(t_full[:text_len, h0:h1])
+            if nvalid < Hg:
+                buf[:text_len, nvalid:].zero_()
             exchange(t_send, group, out=buf[text_len:].view(P, S_loc, Hg, D))
             joint.append(buf.unsqueeze(0))
         o_j = flash_attention(joint[0], joint[1], joint[2], sm_scale)[0]
