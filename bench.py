@@ -18,8 +18,11 @@ convention 4*B*H*S*S*D over the max-over-ranks step time), `e2e` = the same
 through the public API with pinned host inputs copied in and the output
 copied out every step, `roofline` = the attention kernel against the
 measured bf16 peak, `cpu_baseline` = the CPU oracle on a bounded sample;
-`secondary` (N=1) = cfg2, cfg4 and fused pre-step kernel timings, and the
-numpy restatement of vidax's NA scan timed on cfg4 row steps.
+`secondary` = (N=1) cfg2, cfg4 and fused pre-step kernel timings and the
+numpy restatement of vidax's NA scan timed on cfg4 row steps; (every N) one
+Wan2.1-1.3B DiT step at BASELINE config 5, B=1 and the CFG B=2 step, with
+the attention kernels' share; `parity` = seeded rows of the timed output
+against a float32 softmax reference computed on the GPU.
 
 `--impl reference` times the reference's CPU path (vidax's JAX CPU attention
 is `jax.nn.dot_product_attention`; JAX is absent, so its numpy restatement in
@@ -438,68 +441,97 @@ def run_kernel_only(args):
     print(json.dumps(rec), flush=True)
 
 
-def run_dit(args, rank: int, world: int, local_rank: int):
+def dit_measure(world: int, dev, batch: int = 1, steps: int = 3, warmup: int = 2) -> dict:
     """One Wan2.1-1.3B DiT forward step at BASELINE config 5 (latent
-    (1, 21, 60, 104, 16) -> 32760 tokens, 512 text tokens, t = 500; random
-    weights and inputs): Ulysses sequence parallelism over the launched
-    ranks, 12 heads padded to a multiple of the rank count. Prints one JSON
-    line (whole-job matmul TFLOP/s and step time, max over ranks)."""
+    (B, 21, 60, 104, 16) -> 32760 tokens, 512 text tokens, t = 500; random
+    weights and inputs): Ulysses sequence parallelism over the `world` ranks
+    of the default group (axis "sp", registered by the caller when world >
+    1), 12 heads padded to a multiple of the rank count. batch = 2 is the
+    reference's classifier-free-guidance step (conditional and
+    unconditional rows in one batch, generate_wan2_1_t2v.py:453-456).
+    Device time per step with CUDA events, max over ranks, plus the
+    attention kernels' share of it (every self- and cross-attention launch
+    bracketed by events). All ranks must call it together."""
     import torch
     import torch.distributed as dist
     import vidax_b200 as vx
     from vidax_b200 import _lib
+    from vidax_b200 import attention as vx_attention
     from vidax_b200.wan_dit import T2V_1_3B, init_params, step_flops, wan_dit_forward
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    _lib.load()
     cfg = T2V_1_3B
-    sp = None
-    if world > 1:
-        vx.register_axis("sp", None)
-        sp = "sp"
-    p = init_params(cfg, dev, seed=5)
+    sp = "sp" if world > 1 else None
+    p = init_params(cfg, dev, seed=5, on_device=True)
     gen = torch.Generator(device=dev)
     gen.manual_seed(5)
-    latents = torch.randn((1, 21, 60, 104, cfg.in_dim), generator=gen, device=dev).bfloat16()
-    context = torch.randn((1, cfg.text_len, cfg.text_dim), generator=gen, device=dev).bfloat16()
-    t = torch.full((1,), 500.0, device=dev)
+    latents = torch.randn((batch, 21, 60, 104, cfg.in_dim), generator=gen, device=dev).bfloat16()
+    context = torch.randn((batch, cfg.text_len, cfg.text_dim), generator=gen, device=dev).bfloat16()
+    t = torch.full((batch,), 500.0, device=dev)
     rope = vx.rope3d_freqs(21, 30, 52, cfg.head_dim, device=dev)
 
     def step():
         return wan_dit_forward(p, cfg, latents, t, context, rope, sp_axis_name=sp)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     if world > 1:
         dist.barrier()
+    events = []
+    vx_attention.KERNEL_EVENTS = events
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         out = step()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    vx_attention.KERNEL_EVENTS = None
+    ms = e0.elapsed_time(e1) / steps
+    attn_ms = sum(a.elapsed_time(b) for a, b in events) / steps
     if world > 1:
-        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        tt = torch.tensor([ms, attn_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+        ms, attn_ms = float(tt[0]), float(tt[1])
         dist.barrier()
+    fl = batch * step_flops(cfg, 21 * 30 * 52)
+    status = _lib.device_status()
+    shape = list(out.shape)
+    del p, out
+    return {"desc": f"Wan2.1-1.3B DiT forward step (cfg5), B={batch}"
+                    + (" (CFG: conditional + unconditional)" if batch == 2 else "")
+                    + f", 32760 tokens, 30 blocks, {'ulysses-sp%d' % world if world > 1 else 'single GPU'}",
+            "ms": round(ms, 3), "tflops": round(fl / (ms / 1e3) / 1e12, 2),
+            "flops_per_step": fl, "attention_kernel_ms": round(attn_ms, 3),
+            "attention_share": round(attn_ms / ms, 4), "steps": steps, "warmup": warmup,
+            "out_shape": shape, "device_status": status}
+
+
+def run_dit(args, rank: int, world: int, local_rank: int):
+    """--dit: the cfg5 DiT step as the whole benchmark line (B = 1)."""
+    import torch
+    import vidax_b200 as vx
+    from vidax_b200 import _lib
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    if world > 1:
+        vx.register_axis("sp", None)
+    rec = dit_measure(world, dev, batch=1, steps=args.steps, warmup=args.warmup)
+    if world > 1:
         vx.unregister_axis("sp")
-    fl = step_flops(cfg, 21 * 30 * 52)
     if rank == 0:
         print(json.dumps({
-            "metric": "Wan2.1-1.3B DiT forward step (cfg5), matmul TFLOP/s", "value": round(fl / (ms / 1e3) / 1e12, 2),
+            "metric": "Wan2.1-1.3B DiT forward step (cfg5), matmul TFLOP/s", "value": rec["tflops"],
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": rec["ms"], "higher_is_better": True, "scaling": "strong",
             "dtype": "bf16", "data": "synthetic (random weights and inputs)",
             "config": {"workload": "cfg5: Wan2.1-1.3B t2v DiT step, latent (1, 21, 60, 104, 16), "
                                    "32760 tokens, 30 blocks, text 512, CFG off (B=1)",
                        "parallelism": f"ulysses-sp{world}" if world > 1 else "single",
-                       "flops_per_step": fl},
-            "out_shape": list(out.shape), "device_status": _lib.device_status()}), flush=True)
+                       "flops_per_step": rec["flops_per_step"]},
+            "attention_share": rec["attention_share"], "out_shape": rec["out_shape"],
+            "device_status": rec["device_status"]}), flush=True)
 
 
 def run_reference(args, rank: int):
@@ -701,7 +733,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                "frac_of_hbm": round(gbs / hbm, 4), "hbm_peak_source": hbm_src}
         assert _lib.device_status() == 0
 
-    if secondary and not args.no_cpu_baseline:
+    if not args.no_dit:
+        # BASELINE config 5 at this N: one DiT step, B = 1 and the CFG B = 2 step
+        torch.cuda.synchronize()
+        time.sleep(1.0)
+        for bsz in (1, 2):
+            secondary[f"dit_cfg5_b{bsz}"] = dit_measure(world, dev, batch=bsz)
+        assert _lib.device_status() == 0
+
+    if secondary and world == 1 and not args.no_cpu_baseline:
         add_na_cpu_line(secondary, args.cpu_seconds / 2)
 
     cpu = None
@@ -766,6 +806,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the extra cfg2 / cfg4 single-kernel measurements")
+    ap.add_argument("--no-dit", action="store_true",
+                    help="skip the cfg5 DiT step secondary measurement")
     ap.add_argument("--dit", action="store_true",
                     help="time one Wan2.1-1.3B DiT forward step (BASELINE config 5) instead")
     ap.add_argument("--kernel-only", default=None,

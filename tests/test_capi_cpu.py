@@ -164,3 +164,20 @@ def test_glue_and_copy_validation_without_device(lib):
     st.restype = ctypes.c_int
     assert st(0, None) == _lib.VX_EINVAL
     assert st(5_000_000_000, None) == _lib.VX_EINVAL
+
+
+def test_jax_ffi_shim_declares_every_target_and_fails_clearly_without_jax():
+    """The jax.ffi shim: every registered target names a handler the C++
+    source defines; without JAX (this image) register() raises ImportError
+    with a clear message instead of failing later."""
+    import importlib.util
+    import re
+    from vidax_b200 import jax_ffi
+    src = open(jax_ffi.SHIM_SRC).read()
+    handlers = set(re.findall(r"XLA_FFI_DEFINE_HANDLER_SYMBOL\((\w+),", src))
+    assert set(jax_ffi.TARGETS.values()) == handlers
+    for fn in ("vx_attn_fwd", "vx_na3d_fwd", "vx_ulysses_pack", "vx_ulysses_unpack"):
+        assert fn + "(" in src
+    if importlib.util.find_spec("jax") is None:
+        with pytest.raises(ImportError, match="jax"):
+            jax_ffi.register()

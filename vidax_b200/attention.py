@@ -23,6 +23,12 @@ import torch
 from . import _lib
 
 
+#: When set to a list, (start, end) CUDA events bracketing every attention
+#: kernel launch of `flash_attention` are appended to it (kernel-level timing
+#: for benchmarks; the data path is unchanged).
+KERNEL_EVENTS: Optional[list] = None
+
+
 def _check_bshd(name: str, t: torch.Tensor) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
@@ -97,9 +103,16 @@ def flash_attention(
     a.lse = lse.data_ptr() if lse is not None else None
     a.schedule = _lib.VX_SCHED_DYNAMIC if dynamic_schedule else _lib.VX_SCHED_STATIC
     lib = _lib.load()
+    events = KERNEL_EVENTS
     with torch.cuda.device(q.device):
         s = stream if stream is not None else torch.cuda.current_stream(q.device)
+        if events is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
         _lib.check(lib.vx_attn_fwd(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)))
+        if events is not None:
+            e1.record(s)
+            events.append((e0, e1))
     return (out, lse) if return_lse else out
 
 
