@@ -17,6 +17,7 @@
 #include <set>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "attn_sm100.cuh"
 #include "dit_glue.cuh"
@@ -375,21 +376,32 @@ using NaGeoDefault = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW, HD>;
 
 int na_start_host(int i, int L, int k) { return std::min(std::max(i - k / 2, 0), L - k); }
 
-// MMA work (key tiles processed summed over query tiles) of one tiling on a
-// T x H x W grid with effective window (kt, kh, kw); mirrors NaGeo exactly.
-long long na_tiling_cost(const int lim[3], const int ksz[3], const int qbox[3], int pair) {
+// Predicted run time (arbitrary units) of one tiling on a T x H x W grid with
+// effective window (kt, kh, kw); mirrors NaGeo's key-union walk exactly. A
+// CTA walks the union of its two query boxes' windows in key tiles: a tile
+// both boxes need costs a paired step (the two softmax warpgroups ping-pong),
+// a tile only one box needs a solo step (no partner to overlap with), and
+// every unit pays a fixed start-up / epilogue cost. The weights were fitted
+// to measured times of every candidate tiling on B200 (BASELINE config 4 at
+// head_dim 128; LTX-2.5 decoder windows 3x5x5, 3x7x7, 11x11x11 at head_dim
+// 64): the minimum-MMA-work tiling was up to 13 % slower than the best one,
+// this model picks the best within 5 %.
+double na_tiling_cost(const int lim[3], const int ksz[3], const int qbox[3], int pair, int head_dim) {
+  const double w_paired = head_dim == 128 ? 18.0 : 17.0;
+  const double w_solo = head_dim == 128 ? 12.5 : 13.7;
+  const double w_unit = head_dim == 128 ? 111.0 : 27.1;
   const int kvb[3] = {kNaKT, kNaKH, kNaKW};
   int rsz[3], regions[3];
   for (int a = 0; a < 3; ++a) {
     rsz[a] = qbox[a] * (a == pair ? 2 : 1);
     regions[a] = (lim[a] + rsz[a] - 1) / rsz[a];
   }
-  long long cost = 0;
+  long long paired = 0, solo = 0, units = 0;
   for (int rt = 0; rt < regions[0]; ++rt)
     for (int rh = 0; rh < regions[1]; ++rh)
       for (int rw = 0; rw < regions[2]; ++rw) {
         const int reg[3] = {rt, rh, rw};
-        int wu0[2][3], wu1[2][3], cu0[3], cu1[3];
+        int wu0[2][3], wu1[2][3], cu0[3], cu1[3], n_ax[3];
         for (int a = 0; a < 3; ++a) {
           bool first = true;
           for (int t = 0; t < 2; ++t) {
@@ -405,28 +417,39 @@ long long na_tiling_cost(const int lim[3], const int ksz[3], const int qbox[3], 
             }
           }
           if (first) { cu0[a] = cu1[a] = 0; }
+          n_ax[a] = cu1[a] > cu0[a] ? (cu1[a] - cu0[a] + kvb[a] - 1) / kvb[a] : 0;
         }
-        for (int t = 0; t < 2; ++t) {
-          long long tiles = 1;
+        ++units;
+        // per axis, which of the union's tile positions each query box needs
+        std::vector<int> need_ax[2][3];
+        for (int t = 0; t < 2; ++t)
           for (int a = 0; a < 3; ++a) {
-            // key tiles of the CTA grid (aligned at cu0) that meet [wu0, wu1)
-            if (wu1[t][a] <= wu0[t][a]) { tiles = 0; break; }
-            const int first_tile = (wu0[t][a] - cu0[a]) / kvb[a];
-            const int last_tile = (wu1[t][a] - 1 - cu0[a]) / kvb[a];
-            tiles *= (last_tile - first_tile + 1);
+            need_ax[t][a].resize(n_ax[a]);
+            for (int j = 0; j < n_ax[a]; ++j) {
+              const int o = cu0[a] + j * kvb[a];
+              need_ax[t][a][j] = (o < wu1[t][a] && wu0[t][a] < o + kvb[a]) ? 1 : 0;
+            }
           }
-          cost += tiles;
-        }
+        for (int jt = 0; jt < n_ax[0]; ++jt)
+          for (int jh = 0; jh < n_ax[1]; ++jh)
+            for (int jw = 0; jw < n_ax[2]; ++jw) {
+              int need = 0;
+              for (int t = 0; t < 2; ++t)
+                need += need_ax[t][0][jt] & need_ax[t][1][jh] & need_ax[t][2][jw];
+              if (need == 2) ++paired;
+              else if (need == 1) ++solo;
+            }
       }
-  return cost;
+  return w_paired * static_cast<double>(paired) + w_solo * static_cast<double>(solo) +
+         w_unit * static_cast<double>(units);
 }
 
 struct NaChoice { int qbox[3]; int pair; };
 
-NaChoice na_choose_tiling(const int lim[3], const int ksz[3]) {
+NaChoice na_choose_tiling(const int lim[3], const int ksz[3], int head_dim) {
   static std::mutex mu;
-  static std::map<std::array<int, 6>, NaChoice> cache;
-  const std::array<int, 6> key = {lim[0], lim[1], lim[2], ksz[0], ksz[1], ksz[2]};
+  static std::map<std::array<int, 7>, NaChoice> cache;
+  const std::array<int, 7> key = {lim[0], lim[1], lim[2], ksz[0], ksz[1], ksz[2], head_dim};
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -436,10 +459,10 @@ NaChoice na_choose_tiling(const int lim[3], const int ksz[3]) {
                                  {4, 8, 4}, {8, 4, 4},  {1, 4, 32}, {2, 16, 4}, {1, 2, 64},
                                  {8, 2, 8}, {4, 2, 16}, {1, 32, 4}, {16, 2, 4}, {2, 2, 32}};
   NaChoice best = {{2, 8, 8}, 0};
-  long long best_cost = -1;
+  double best_cost = -1;
   for (const auto& c : cands)
     for (int pair = 0; pair < 3; ++pair) {
-      const long long cost = na_tiling_cost(lim, ksz, c, pair);
+      const double cost = na_tiling_cost(lim, ksz, c, pair, head_dim);
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
         best = {{c[0], c[1], c[2]}, pair};
@@ -534,7 +557,7 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
   }
   NaChoice ch;
   if (a->q_box[0] == 0 && a->q_box[1] == 0 && a->q_box[2] == 0) {
-    ch = na_choose_tiling(lim, ksz);
+    ch = na_choose_tiling(lim, ksz, a->head_dim);
   } else {
     for (int i = 0; i < 3; ++i) {
       if (!is_pow2(a->q_box[i])) return fail(VX_EINVAL, "q_box entries must be powers of two");
