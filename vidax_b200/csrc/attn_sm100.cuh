@@ -483,14 +483,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_used = m_new;
         }
         const float neg_m = (m_used == neg_inf()) ? 0.f : -m_used;
-        // p = 2^(s * scale_log2 - m) on MUFU, packed to bf16 over S's columns
+        // p = 2^(s * scale_log2 - m) on MUFU, packed to bf16 over S's columns.
+        // Even columns sum into ls0, odd into ls1. Geometries whose softmax is
+        // issue-bound (the neighborhood one, with its masks) do the scaling
+        // and the sums two columns per instruction (f32x2); the results are
+        // bit-identical (same roundings, same summation order).
         float ls0 = 0.f, ls1 = 0.f;
+        uint64_t ls2 = f2_pack(0.f, 0.f);
+        const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(neg_m, neg_m);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
           if (!((active >> c) & 1u)) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          } else if (Geo::kPackedSoftmax) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])),
+                               sc2, nm2), x0, x1);
+              const float e0 = ex2_approx(x0);
+              const float e1 = ex2_approx(x1);
+              ls2 = f2_add(ls2, f2_pack(e0, e1));
+              pk[i] = pack_bf16x2(e0, e1);
+            }
           } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -504,6 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st16(t_s + c * 16, pk);
         }
+        if (Geo::kPackedSoftmax) f2_unpack(ls2, ls0, ls1);
         if (rescale_o) {
           // O is complete up to this query tile's previous KV tile: S(j) was
           // issued after that PV and its commit tracks every earlier MMA.
@@ -587,6 +605,7 @@ struct DenseParams {
 template <int HD>
 struct DenseGeo {
   static constexpr int kHeadDim = HD;
+  static constexpr bool kPackedSoftmax = false;  // MUFU-bound: scalar arithmetic is as fast
   using Params = DenseParams;
   const DenseParams& p;
   int b, h, hk, q0, kv_valid;
@@ -725,6 +744,7 @@ __device__ __forceinline__ uint32_t bit_range(int lo, int hi, int n) {
 template <int KT, int KH, int KW, int HD>
 struct NaGeo {
   static constexpr int kHeadDim = HD;
+  static constexpr bool kPackedSoftmax = true;  // issue-bound (masks): two columns per instruction
   static_assert(KT * KH * KW == 128, "key tile must hold 128 keys");
   static_assert(KW == 8 || KW == 16 || KW == 32, "key tile width 8, 16 or 32");
   using Params = NaParams;
@@ -880,6 +900,12 @@ struct NaGeo {
   // chunk (cm[c] bit i: column 32c + i). Returns the chunks (bit c) with a
   // visible column in any row of this warp: the softmax skips the others (no
   // mask, no exponentials; P is zero there).
+  //
+  // For KW == 16 (the instantiated key tile) every chunk is two (ct, ch) rows
+  // of 16 columns that share this row's window columns, so the masks are kept
+  // factored: cm[0] = the 16-bit column mask, cm[1] bit r = (ct, ch) row r of
+  // the tile (r = ct * KH + ch) is in the window; apply_masks then adds 0 or
+  // -inf biases two columns per instruction instead of selecting per column.
   __device__ uint32_t chunk_masks(int j, uint32_t (&cm)[4]) const {
     int o[3];
     tile_origin(j, o);
@@ -888,6 +914,20 @@ struct NaGeo {
     const uint32_t wmask = bit_range(ws[2] - o[2], ws[2] + p.kw - o[2], KW);
     constexpr int kRowsPerChunk = 32 / KW;  // (ct, ch) rows of the tile per chunk (>= 1)
     uint32_t active = 0;
+    if constexpr (KW == 16) {
+      uint32_t rows = 0;
+#pragma unroll
+      for (int r = 0; r < KT * KH; ++r)
+        if (((tmask >> (r / KH)) & 1u) && ((hmask >> (r % KH)) & 1u)) rows |= 1u << r;
+      if (!row_valid || wmask == 0u) rows = 0;
+      cm[0] = wmask;
+      cm[1] = rows;
+      cm[2] = cm[3] = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (__any_sync(0xffffffffu, ((rows >> (2 * c)) & 3u) != 0u)) active |= 1u << c;
+      return active;
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t m = 0;
@@ -908,6 +948,38 @@ struct NaGeo {
   // rounding of q.k); inactive chunks are left as they are.
   __device__ void apply_masks(const uint32_t (&cm)[4], uint32_t active,
                               uint32_t (&sr)[4][32]) const {
+    if constexpr (KW == 16) {
+      const float ninf = neg_inf();
+      uint64_t wb[8];  // column biases, two columns per register pair
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        wb[k] = f2_pack(((cm[0] >> (2 * k)) & 1u) ? 0.f : ninf,
+                        ((cm[0] >> (2 * k + 1)) & 1u) ? 0.f : ninf);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (!((active >> c) & 1u)) continue;
+        if (p.round_logits) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            sr[c][i] = __float_as_uint(__bfloat162float(__float2bfloat16_rn(__uint_as_float(sr[c][i]))));
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const float rb = ((cm[1] >> (2 * c + r)) & 1u) ? 0.f : ninf;
+          const uint64_t rb2 = f2_pack(rb, rb);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int i = 16 * r + 2 * k;
+            float a, bq;
+            f2_unpack(f2_add(f2_add(f2_pack(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1])),
+                                    wb[k]), rb2), a, bq);
+            sr[c][i] = __float_as_uint(a);
+            sr[c][i + 1] = __float_as_uint(bq);
+          }
+        }
+      }
+      return;
+    }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       if (!((active >> c) & 1u)) continue;
