@@ -926,8 +926,7 @@ struct NaGeo {
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         if (__any_sync(0xffffffffu, ((rows >> (2 * c)) & 3u) != 0u)) active |= 1u << c;
-      return active;
-    }
+    } else {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t m = 0;
@@ -941,6 +940,7 @@ struct NaGeo {
       if (!row_valid) m = 0;
       cm[c] = m;
       if (__any_sync(0xffffffffu, m != 0u)) active |= 1u << c;
+    }
     }
     return active;
   }
@@ -978,8 +978,7 @@ struct NaGeo {
           }
         }
       }
-      return;
-    }
+    } else {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       if (!((active >> c) & 1u)) continue;
@@ -990,6 +989,7 @@ struct NaGeo {
       }
 #pragma unroll
       for (int i = 0; i < 32; ++i) sr[c][i] = ((cm[c] >> i) & 1u) ? sr[c][i] : 0xff800000u;
+    }
     }
   }
   __device__ __nv_bfloat16* row_ptr() const {
