@@ -187,8 +187,7 @@ typedef struct vx_na3d_args {
   float scale;
   int32_t round_logits;
   int32_t q_box[3];    /* query tile box (t, h, w), product 128; all 0 = choose automatically */
-  int32_t pair_axis;   /* axis along which a CTA pairs two query boxes (0-2), or 3: no pairing, each
-                          CTA runs two independent streams of single boxes; ignored when q_box is 0 */
+  int32_t pair_axis;   /* axis along which a CTA pairs two query boxes; ignored when q_box is 0 */
 } vx_na3d_args;
 
 int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);

@@ -53,9 +53,7 @@ def test_na3d_matches_oracle(shape, kernel):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("q_box,pair", [((2, 8, 8), 0), ((1, 8, 16), 2), ((4, 4, 8), 1),
-                                        ((1, 2, 64), 0), ((8, 4, 4), 2),
-                                        # pair 3: two streams of single boxes per CTA
-                                        ((2, 8, 8), 3), ((4, 4, 8), 3), ((1, 8, 16), 3)])
+                                        ((1, 2, 64), 0), ((8, 4, 4), 2)])
 def test_na3d_every_tiling_agrees(q_box, pair):
     """Every query tiling gives the oracle's result (tiling is a schedule choice only)."""
     import vidax_b200 as vx
@@ -221,27 +219,3 @@ def test_na3d_time_sharded_two_gpus_nccl():
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "NA SP OK" in res.stdout
 
-
-@pytest.mark.gpu
-@pytest.mark.parametrize("shape,kernel,hd", [((2, 5, 11, 19, 3), (3, 5, 7), 128),
-                                             ((1, 9, 20, 33, 4), (5, 9, 9), 128),
-                                             ((1, 4, 16, 24, 5), (3, 7, 7), 64),
-                                             ((1, 3, 6, 9, 2), (11, 11, 11), 64)])
-def test_na3d_two_stream_schedule_matches_paired(shape, kernel, hd):
-    """The two-stream schedule (pair_axis 3: each CTA runs two independent
-    streams of single query boxes, odd unit counts included) against the
-    paired schedule and the oracle. The two group a row's keys into key tiles
-    from different origins near clamped borders, so the float sums may round
-    differently: the bar is closeness, not identical bits."""
-    import vidax_b200 as vx
-    B, T, H, W, NH = shape
-    q, k, v = seeded_qkv((B, T, H, W, NH, hd), 900 + T * 3 + W + hd, n=3)
-    q = to_bf16(q * np.float32(hd ** -0.5))
-    tq, tk, tv = _dev(q), _dev(k), _dev(v)
-    o_pair = vx.neighborhood_attention_3d(tq, tk, tv, kernel, q_box=(2, 8, 8), pair_axis=0)
-    o_str = vx.neighborhood_attention_3d(tq, tk, tv, kernel, q_box=(2, 8, 8), pair_axis=3)
-    torch.cuda.synchronize()
-    assert _status_clean()
-    assert float((o_pair.float() - o_str.float()).abs().max()) <= 1e-2
-    mx, mean = compare(o_str.float().cpu().numpy(), na3d(q, k, v, kernel))
-    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)

@@ -21,7 +21,6 @@
 
 #include "attn_sm100.cuh"
 #include "dit_glue.cuh"
-#include "na_stream_sm100.cuh"
 #include "norm_rope_pack.cuh"
 #include "ulysses_pack.cuh"
 
@@ -565,9 +564,7 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
       ch.qbox[i] = a->q_box[i];
     }
     if (ch.qbox[0] * ch.qbox[1] * ch.qbox[2] != 128) return fail(VX_EINVAL, "q_box must hold 128 queries");
-    if (a->pair_axis < 0 || a->pair_axis > 3)
-      return fail(VX_EINVAL, "pair_axis must be 0, 1, 2 or 3 (3: no pairing, two streams of single "
-                  "query boxes per CTA)");
+    if (a->pair_axis < 0 || a->pair_axis > 2) return fail(VX_EINVAL, "pair_axis must be 0, 1 or 2");
     ch.pair = a->pair_axis;
   }
 
@@ -629,24 +626,7 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
   p.round_logits = a->round_logits ? 1 : 0;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (ch.pair == 3) {
-    // No pairing: units are single query boxes, and every CTA runs two
-    // independent streams of them (na_stream_kernel), units 2c + t + 2kG.
-    int sms = 0;
-    if ((rc = num_sms(dev, &sms)) != VX_OK) return rc;
-    dim3 grid(static_cast<unsigned>(std::min<long long>((units + 1) / 2, sms)));
-    if (HD == 128) {
-      auto kern = vx::na_stream::na_stream_kernel<128>;
-      constexpr uint32_t smem = vx::na_stream::Layout<128>::kSmemBytes;
-      if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
-      kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
-    } else {
-      auto kern = vx::na_stream::na_stream_kernel<64>;
-      constexpr uint32_t smem = vx::na_stream::Layout<64>::kSmemBytes;
-      if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
-      kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
-    }
-  } else {
+  {
     // One CTA per unit, and each resident CTA also claims not-yet-launched
     // units through cluster launch control: the next unit's loads overlap the
     // current unit's tail (5 % faster than one unit per CTA, measured; a static
