@@ -300,11 +300,11 @@ def parity_sample(out, q, k, v, world: int, dev, rows_per_rank: int = 32) -> dic
     import torch.distributed as dist
     b, s_loc, h, d = q.shape
     if world > 1:
-        kg = torch.empty((world,) + tuple(k.shape[1:]), dtype=k.dtype, device=dev)
+        # (world * s_loc, H, D): the ranks' chunks in rank order
+        kg = torch.empty((world * s_loc, h, d), dtype=k.dtype, device=dev)
         vg = torch.empty_like(kg)
         dist.all_gather_into_tensor(kg, k[0].contiguous())
         dist.all_gather_into_tensor(vg, v[0].contiguous())
-        kg, vg = kg.reshape(-1, h, d), vg.reshape(-1, h, d)
     else:
         kg, vg = k[0], v[0]
     gen = torch.Generator().manual_seed(11)

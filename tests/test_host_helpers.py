@@ -168,3 +168,59 @@ def test_fully_masked_rows_modes():
     bias3[1, 0, 0, 0] = -2e9
     with pytest.raises(NotImplementedError):
         _fully_masked_rows(bias3, None, _key_lengths_from_bias(bias3, B, Sk), B, Sk)
+
+
+def _parity_worker(rank, world, port, errq):
+    import os
+    import torch
+    import torch.distributed as dist
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        import bench
+        g = torch.Generator().manual_seed(5)
+        S_loc, H, D = 40, 3, 16
+        q, k, v = (torch.randn((world, S_loc, H, D), generator=g).bfloat16() for _ in range(3))
+        # the global sequence is the ranks' chunks in rank order
+        qg, kg, vg = (t.reshape(1, world * S_loc, H, D) for t in (q, k, v))
+        p = torch.softmax(torch.einsum("bqhd,bkhd->bhqk", qg.float(), kg.float()) * D ** -0.5, -1)
+        o = torch.einsum("bhqk,bkhd->bqhd", p, vg.float()).bfloat16()
+        sl = slice(rank * S_loc, (rank + 1) * S_loc)
+        rec = bench.parity_sample(o[:, sl], qg[:, sl], kg[:, sl], vg[:, sl], world,
+                                  torch.device("cpu"), rows_per_rank=8)
+        assert rec["pass"] and rec["max_abs"] < 2e-2, rec
+        # a wrong output on one rank fails every rank's verdict (max over ranks)
+        bad = o[:, sl].clone()
+        if rank == 1:
+            bad += 0.5
+        rec = bench.parity_sample(bad, qg[:, sl], kg[:, sl], vg[:, sl], world,
+                                  torch.device("cpu"), rows_per_rank=8)
+        assert not rec["pass"], rec
+        dist.destroy_process_group()
+    except BaseException as e:  # noqa: BLE001
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+
+
+def test_bench_parity_sample_over_ranks():
+    """bench.py's parity self-check at N > 1 (gloo on CPU): each rank checks
+    its rows against the ranks' gathered keys / values, the verdict is the
+    max over ranks."""
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    procs = [ctx.Process(target=_parity_worker, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs)
