@@ -2,10 +2,14 @@
  * vidax_cuda.h -- C ABI of libvidax_cuda.so, the B200 (sm_100a) implementation
  * of vidax's attention hot path.
  *
- * Every entry point takes plain device pointers, sizes and element strides
- * and a CUDA stream; none allocates or frees caller memory, none synchronises
- * the host. Return value: VX_OK or a VX_E* code; vx_last_error() gives the
- * message of the last failure on the calling thread.
+ * Every compute entry point takes plain device pointers, sizes and element
+ * strides and a CUDA stream; none allocates or frees device memory, none
+ * synchronises the host. The exceptions are the communicator handles
+ * (vx_comm_init / vx_comm_wrap create a host object, an internal stream and
+ * events; vx_comm_destroy waits for that stream) and the status / self-test
+ * calls, which synchronise. Return value: VX_OK or a VX_E* code;
+ * vx_last_error() gives the message of the last failure on the calling
+ * thread.
  *
  * Layouts follow vidax: attention tensors are BSHD (batch, seq, heads,
  * head_dim) with head_dim contiguous; neighborhood tensors are
@@ -27,7 +31,7 @@ enum {
   VX_EINVAL = 1,        /* bad argument: shape, stride, alignment, null pointer */
   VX_EUNSUPPORTED = 2,  /* valid request this build does not implement */
   VX_ECUDA = 3,         /* CUDA runtime / driver error */
-  VX_ENCCL = 4,         /* reserved (NCCL error): the library itself calls no collective */
+  VX_ENCCL = 4,         /* NCCL error (vx_comm_*, vx_ulysses_attn_fwd) */
   VX_ETIMEOUT = 5,      /* a bounded device-side wait expired (see vx_device_status) */
 };
 
@@ -114,6 +118,61 @@ typedef struct vx_head_slab_args {
 int vx_ulysses_pack(const vx_head_slab_args* args, vx_stream_t stream);
 /* contiguous (groups, seq, hg, D) -> strided (seq, heads, D) rows */
 int vx_ulysses_unpack(const vx_head_slab_args* args, vx_stream_t stream);
+
+/* ----------------------------------------------------------------------
+ * The whole DeepSpeed-Ulysses layer behind one call, over an NCCL
+ * communicator: replaces sequence_parallel_self_attention
+ * (src/vidax/core/attention.py:341-388) -- the tokens->heads all_to_all of
+ * q, k, v (:379-381), local attention over the full sequence for this rank's
+ * head group (:383-386), the heads->tokens all_to_all (:388) -- for hosts
+ * without the torch mirror (vidax_b200.ulysses). The rank's head group
+ * (ceil(heads / world) heads, zero heads past `heads`) is processed in
+ * pipelined slices: slice j+1's exchange runs on an internal stream while
+ * the attention kernel computes slice j, and slice j's reverse exchange
+ * overlaps slice j+1. All work is ordered after prior work on `stream` and
+ * complete before later work on it; the host does not block.
+ *
+ * NCCL is not linked: its entry points are looked up at run time in the
+ * NCCL already loaded in the process (e.g. by torch), else libnccl.so.2.
+ * A vx_comm wraps either the caller's communicator (vx_comm_wrap, e.g.
+ * torch's ProcessGroupNCCL communicator; not destroyed here) or one created
+ * from a unique id every rank received from rank 0 (vx_comm_init: the
+ * vx_comm_* entry points of the C ABI this library proposes for a JAX host,
+ * which has no NCCL communicator of its own to lend).
+ */
+typedef struct vx_comm vx_comm;
+typedef struct vx_ulysses_args {
+  const void* q;  /* (B, S_loc, H, D) bf16: this rank's tokens [r*S_loc, (r+1)*S_loc) */
+  const void* k;
+  const void* v;
+  void* o;        /* (B, S_loc, H, D) bf16 */
+  int64_t q_stride[3]; /* element strides of (b, s, h); d stride 1, multiples of 8 */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int32_t batch, seq_local, heads, head_dim;
+  float scale;          /* softmax scale, > 0 */
+  int32_t valid_len;    /* 0: all world * seq_local tokens are real; else keys >= valid_len are
+                           padding, invisible to every query (the sequence padded to a multiple
+                           of the world size) */
+  void* workspace;      /* device memory, 256-byte aligned, vx_ulysses_workspace_size bytes; only
+                           one call may use it at a time */
+  int64_t workspace_bytes;
+} vx_ulysses_args;
+
+/* NCCL unique id (128 bytes) for vx_comm_init, made on one rank and sent to
+ * every other rank by the host. */
+int vx_comm_get_unique_id(char uid_out[128]);
+/* Creates this rank's communicator (collective: every rank calls it, each on
+ * its own GPU, current at the call). */
+int vx_comm_init(int32_t rank, int32_t world, const char uid[128], vx_comm** comm_out);
+/* Wraps an existing ncclComm_t of the current device (borrowed). */
+int vx_comm_wrap(void* nccl_comm, vx_comm** comm_out);
+/* Releases the wrapper (and the communicator if vx_comm_init made it). */
+int vx_comm_destroy(vx_comm* comm);
+/* Workspace bytes a call with these arguments needs on a `world`-rank axis. */
+int vx_ulysses_workspace_size(const vx_ulysses_args* args, int32_t world, int64_t* bytes_out);
+int vx_ulysses_attn_fwd(const vx_ulysses_args* args, vx_comm* comm, vx_stream_t stream);
 
 /* ----------------------------------------------------------------------
  * Fused pre-attention step: RMSNorm + 3-D RoPE + head-slab pack, one HBM

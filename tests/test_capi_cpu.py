@@ -181,3 +181,22 @@ def test_jax_ffi_shim_declares_every_target_and_fails_clearly_without_jax():
     if importlib.util.find_spec("jax") is None:
         with pytest.raises(ImportError, match="jax"):
             jax_ffi.register()
+
+
+def test_ulysses_layer_workspace_size_without_device(lib):
+    """vx_ulysses_workspace_size is host arithmetic: 256 bytes + 8 slabs of
+    world x S_loc x ceil(H / world) x D bf16 (q, k, v sent and received, the
+    attention output sent and received), each padded to 256 bytes."""
+    from vidax_b200.ulysses_capi import UlyssesArgs
+    a = UlyssesArgs()
+    a.batch, a.seq_local, a.heads, a.head_dim = 1, 9450, 40, 128
+    n = ctypes.c_int64(0)
+    f = lib.vx_ulysses_workspace_size
+    f.argtypes = [ctypes.POINTER(UlyssesArgs), ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)]
+    f.restype = ctypes.c_int
+    assert f(ctypes.byref(a), 8, ctypes.byref(n)) == 0
+    assert n.value == 256 + 8 * 8 * 9450 * 5 * 128 * 2
+    a.heads = 12  # 12 heads on 8 ranks: ceil -> 2 per rank (zero heads)
+    assert f(ctypes.byref(a), 8, ctypes.byref(n)) == 0
+    assert n.value == 256 + 8 * (-(-(8 * 9450 * 2 * 128 * 2) // 256) * 256)
+    assert f(ctypes.byref(a), 0, ctypes.byref(n)) != 0

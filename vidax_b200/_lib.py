@@ -37,6 +37,12 @@ EXPORTED_SYMBOLS = (
     "vx_gated_residual",
     "vx_memcpy_rows_async",
     "vx_selftest_wait_timeout",
+    "vx_comm_get_unique_id",
+    "vx_comm_init",
+    "vx_comm_wrap",
+    "vx_comm_destroy",
+    "vx_ulysses_workspace_size",
+    "vx_ulysses_attn_fwd",
 )
 
 

@@ -21,7 +21,7 @@ LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libvidax_cuda.so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["vidax_cuda.cu"]
+SOURCES = ["vidax_cuda.cu", "ulysses_layer.cu"]
 
 
 def nvcc_path() -> str:
@@ -51,7 +51,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     tmp = LIB_PATH + ".tmp"
     cmd = [nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-shared",
            "-Xcompiler", "-fPIC", "-I" + INCLUDE, "-I" + CSRC,
-           "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES]
+           "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES] + ["-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

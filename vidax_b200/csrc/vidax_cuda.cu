@@ -5,6 +5,7 @@
 // configuration and the per-device status word the kernels report bounded-
 // wait timeouts into. Nothing here allocates device memory.
 #include "vidax_cuda.h"
+#include "vx_internal.h"
 
 #include <cstdarg>
 #include <cstdio>
@@ -46,6 +47,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 }  // namespace
+
+int vx_internal_fail(int code, const char* msg) { return fail(code, "%s", msg); }
 
 // Device status word: kernels OR timeout codes into it (one instance per
 // device context).

@@ -1,0 +1,6 @@
+// Library-internal helpers shared by the translation units of libvidax_cuda.so.
+#pragma once
+
+// Records `msg` as the calling thread's last error (vx_last_error) and
+// returns `code`.
+int vx_internal_fail(int code, const char* msg);
