@@ -173,6 +173,24 @@ int vx_comm_destroy(vx_comm* comm);
 /* Workspace bytes a call with these arguments needs on a `world`-rank axis. */
 int vx_ulysses_workspace_size(const vx_ulysses_args* args, int32_t world, int64_t* bytes_out);
 int vx_ulysses_attn_fwd(const vx_ulysses_args* args, vx_comm* comm, vx_stream_t stream);
+/* vx_ulysses_attn_fwd for callers that may not allocate device memory: an
+ * XLA custom call, for one, whose device memory belongs to XLA's allocator
+ * (which reserves most of it up front), so a cudaMalloc inside the handler
+ * can fail and synchronizes the device. No counterpart in the reference:
+ * its JAX layer gets scratch from XLA.
+ *
+ * Same layer and results as vx_ulysses_attn_fwd; `workspace` and
+ * `workspace_bytes` are ignored. The workspace is instead a built-in 32 MiB
+ * device array (every GPU on which this library's device code is loaded
+ * holds it until the process exits); a call whose vx_ulysses_workspace_size
+ * exceeds 32 MiB fails with VX_EINVAL. The entry point allocates nothing.
+ * The first call on a device looks the array's address up (once per device,
+ * that device current); make that first call before any stream capture.
+ * Every call on a device shares the array: calls that may overlap on the GPU
+ * (on different streams, or from several threads) race on it, so issue them
+ * in order on one stream. Nothing in it needs clearing: each call writes
+ * every workspace byte it reads. */
+int vx_ulysses_attn_fwd_static(const vx_ulysses_args* args, vx_comm* comm, vx_stream_t stream);
 
 /* ----------------------------------------------------------------------
  * Fused pre-attention step: RMSNorm + 3-D RoPE + head-slab pack, one HBM

@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "vx_comm_destroy",
     "vx_ulysses_workspace_size",
     "vx_ulysses_attn_fwd",
+    "vx_ulysses_attn_fwd_static",
 )
 
 

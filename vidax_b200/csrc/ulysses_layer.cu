@@ -161,6 +161,36 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+// Built-in workspace of vx_ulysses_attn_fwd_static, for callers that may not
+// allocate device memory. One instance per GPU on which this library's
+// device code is loaded, held until the process exits; every call on that
+// GPU shares it.
+constexpr int64_t kStaticWorkspaceBytes = 32ll << 20;
+static __device__ __align__(256) unsigned char g_ulysses_static_ws[kStaticWorkspaceBytes];
+
+namespace {
+
+// Device address of g_ulysses_static_ws on the current device `dev`, looked
+// up once per device. In host code the array's name is a host-side shadow,
+// not a device address, so it is never handed to a kernel directly.
+int static_workspace(int dev, void** out) {
+  static std::mutex mu;
+  static std::vector<void*> addr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev < 0) return fail_msg(VX_EINVAL, "bad device");
+  if (static_cast<size_t>(dev) >= addr.size()) addr.resize(dev + 1, nullptr);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ulysses_static_ws);
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetSymbolAddress(built-in Ulysses workspace)");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return VX_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int vx_comm_get_unique_id(char uid_out[128]) {
@@ -391,6 +421,34 @@ int vx_ulysses_attn_fwd(const vx_ulysses_args* a, vx_comm* c, vx_stream_t stream
     }
   }
   return VX_OK;
+}
+
+int vx_ulysses_attn_fwd_static(const vx_ulysses_args* a, vx_comm* c, vx_stream_t stream) {
+  if (a == nullptr || c == nullptr) return fail_msg(VX_EINVAL, "NULL argument");
+  int64_t need = 0;
+  int rc = vx_ulysses_workspace_size(a, c->world, &need);
+  if (rc != VX_OK) return rc;
+  if (need > kStaticWorkspaceBytes) {
+    char buf[256];
+    snprintf(buf, sizeof(buf),
+             "this call needs %lld bytes of workspace; the built-in workspace holds %lld "
+             "(32 MiB): pass a workspace to vx_ulysses_attn_fwd instead",
+             static_cast<long long>(need), static_cast<long long>(kStaticWorkspaceBytes));
+    return fail_msg(VX_EINVAL, buf);
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+  if (dev != c->device) return fail_msg(VX_EINVAL, "the communicator belongs to another device");
+  void* ws = nullptr;
+  if ((rc = static_workspace(dev, &ws)) != VX_OK) return rc;
+  // The layer writes every workspace byte it reads in the same call (the key
+  // count, the zero-filled padding heads of the packed slabs), so nothing
+  // needs clearing between calls.
+  vx_ulysses_args b = *a;
+  b.workspace = ws;
+  b.workspace_bytes = kStaticWorkspaceBytes;
+  return vx_ulysses_attn_fwd(&b, c, stream);
 }
 
 }  // extern "C"
