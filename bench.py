@@ -580,7 +580,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
     import vidax_b200 as vx
-    from vidax_b200 import _lib, ulysses
+    from vidax_b200 import _lib, ulysses, ulysses_peer
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -608,6 +608,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             e1.record()
             ulysses_events.append((e0, e1))
             return o
+        if args.exchange == "peer":
+            return ulysses_peer.sequence_parallel_self_attention_peer(qq, kk, vv)
         return vx.sequence_parallel_self_attention(qq, kk, vv, "sp")
 
     def barrier():
@@ -657,7 +659,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     launch_flops = flops(B, hg, S_GLOBAL, S_GLOBAL, D)
     achieved = launch_flops / (kern_avg / 1e3) / 1e12
     burst, sustained, peak_src = load_peaks()
-    gpu_launches = args.steps * (1 if world == 1 else ulysses.launches_per_layer(H, world, B))
+    per_layer = (ulysses_peer.launches_per_layer(H, world, B) if args.exchange == "peer"
+                 else ulysses.launches_per_layer(H, world, B))
+    gpu_launches = args.steps * (1 if world == 1 else per_layer)
 
     # ---- end to end through the public API: pinned host in, host out
     hq = q.cpu().pin_memory()
@@ -703,6 +707,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         # one q-sized exchange (padded heads) on its own, for the NVLink figure
         a2a = measure_all_to_all(B * s_loc * (-(-H // world) * world) * D, 10, dev,
                                  torch.bfloat16)
+        if args.exchange == "peer":
+            a2a = {"nccl_all_to_all": a2a,
+                   "peer_pack": ulysses_peer.measure_exchange(q[0], 10)}
+            a2a["ms"] = a2a["peer_pack"]["ms"]
 
     secondary = {}
     if world == 1 and not args.no_secondary:
@@ -755,6 +763,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     if world > 1:
         vx.unregister_axis("sp")
+        if args.exchange == "peer":
+            ulysses_peer.release_workspaces()   # collective: every rank, before returning
     if rank != 0:
         return
     traffic = None
@@ -768,6 +778,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": S_GLOBAL, "heads": H,
                    "head_dim": D, "parallelism": f"ulysses-sp{world}" if world > 1 else "single",
+                   "exchange": (args.exchange if world > 1 else None),
                    "l2": "inputs larger than L2 (774 MB per tensor), no flush"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
@@ -793,6 +804,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         line["a2a"] = {"bytes_sent_per_gpu": a2a_bytes,
                        "single_exchange": a2a,
                        "layer_a2a_ms_if_serial": round(4 * a2a["ms"], 4),
+                       "exchange": args.exchange,
                        "note": "4 all-to-alls (q, k, v, o) per layer, pipelined by head "
                                f"slices against the kernel; NVLink {NVLINK_NOMINAL_GBS:.0f} "
                                f"GB/s/dir nominal, {NVLINK_MEASURED_GBS:.0f} measured peer copy"}
@@ -807,6 +819,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
+                    help="N > 1: the Ulysses all-to-alls over NCCL, or done by the slab "
+                         "kernels over NVLink peer memory (vidax_b200.ulysses_peer)")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the extra cfg2 / cfg4 single-kernel measurements")
     ap.add_argument("--no-dit", action="store_true",

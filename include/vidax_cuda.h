@@ -6,7 +6,8 @@
  * strides and a CUDA stream; none allocates or frees device memory, none
  * synchronises the host. The exceptions are the communicator handles
  * (vx_comm_init / vx_comm_wrap create a host object, an internal stream and
- * events; vx_comm_destroy waits for that stream) and the status / self-test
+ * events; vx_comm_destroy waits for that stream), vx_ipc_open / vx_ipc_close
+ * (map / unmap another process's allocation) and the status / self-test
  * calls, which synchronise. Return value: VX_OK or a VX_E* code;
  * vx_last_error() gives the message of the last failure on the calling
  * thread.
@@ -44,7 +45,8 @@ const char* vx_last_error(void);
 /*
  * Reads (and optionally clears) the device status word of the current CUDA
  * device: 0 when every kernel ran to completion, else an OR of
- * 1 (load wait timed out), 2 (MMA wait), 4 (softmax wait), 8 (drain).
+ * 1 (load wait timed out), 2 (MMA wait), 4 (softmax wait), 8 (drain),
+ * 32 (a vx_peer_barrier wait).
  * Synchronises the device. Returns VX_OK or VX_ECUDA.
  */
 int vx_device_status(int* status_out, int clear);
@@ -118,6 +120,60 @@ typedef struct vx_head_slab_args {
 int vx_ulysses_pack(const vx_head_slab_args* args, vx_stream_t stream);
 /* contiguous (groups, seq, hg, D) -> strided (seq, heads, D) rows */
 int vx_ulysses_unpack(const vx_head_slab_args* args, vx_stream_t stream);
+
+/* ----------------------------------------------------------------------
+ * The Ulysses all-to-alls done by the slab kernels over NVLink: replaces
+ * the tiled jax.lax.all_to_all pair of sequence_parallel_self_attention
+ * (src/vidax/core/attention.py:379-381 tokens->heads, :388 heads->tokens)
+ * for ranks on one NVLink / NVSwitch domain whose buffers are mapped into
+ * each other's processes (vx_ipc_*).
+ *
+ * vx_ulysses_pack_peers is vx_ulysses_pack with group g's packed chunk
+ * (seq, hg, D) stored straight to peer[t][g] -- the slot of this rank's
+ * chunk in rank g's receive slab -- instead of to slab.dst: packing and the
+ * tokens->heads exchange in one pass of SM stores over NVLink.
+ * vx_ulysses_unpack_peers is vx_ulysses_unpack reading group g's chunk
+ * straight from peer[t][g] -- this rank's tokens in rank g's attention
+ * output -- into the strided rows at slab.dst: the heads->tokens exchange
+ * and the unpack in one pass of loads over NVLink. Order with the other
+ * ranks' work through vx_peer_barrier. */
+typedef struct vx_peer_slab_args {
+  vx_head_slab_args slab; /* as for vx_ulysses_pack / vx_ulysses_unpack; pack ignores slab.dst,
+                             unpack ignores slab.src */
+  void* peer[3][8];       /* per tensor t and group g < slab.groups (<= 8): the remote chunk */
+  int32_t max_ctas;       /* CTA budget over all groups and tensors; 0 = as many as the data
+                             fills. A small budget leaves SMs to a concurrent kernel. */
+} vx_peer_slab_args;
+int vx_ulysses_pack_peers(const vx_peer_slab_args* args, vx_stream_t stream);
+int vx_ulysses_unpack_peers(const vx_peer_slab_args* args, vx_stream_t stream);
+
+/* Barrier of `world` ranks (one GPU each) through flags in their memory:
+ * each rank writes `epoch` into slot `rank` of every rank's flag array
+ * (after a system-scope fence, so the peer stores of the kernels before it
+ * on `stream` are visible first), then waits until every slot of its own
+ * array holds at least `epoch`. Stream-ordered: later work on `stream` sees
+ * what the other ranks wrote before their arrival. Each flag array is used
+ * by one sequence of barriers, issued in the same order on every rank, with
+ * epoch = 1, 2, ... The wait is bounded by timeout_ns (0: 2 s); on expiry
+ * the kernel sets VX_DEV_TIMEOUT_PEER in the device status word
+ * (vx_device_status) and returns. */
+typedef struct vx_peer_barrier_args {
+  uint32_t* flags[8];  /* flags[g]: rank g's array of `world` uint32 (flags[rank] is local) */
+  int32_t rank, world;
+  uint32_t epoch;
+  int64_t timeout_ns;
+} vx_peer_barrier_args;
+int vx_peer_barrier(const vx_peer_barrier_args* args, vx_stream_t stream);
+#define VX_DEV_TIMEOUT_PEER 32
+
+/* CUDA IPC of device memory allocated with cudaMalloc (torch's default
+ * allocator included): the 64-byte handle of the allocation holding
+ * dev_ptr and dev_ptr's offset in it; another process opens the handle
+ * (mapping the allocation, peer access enabled on first use) and adds the
+ * offset; vx_ipc_close unmaps. */
+int vx_ipc_get_handle(const void* dev_ptr, char handle_out[64], int64_t* offset_out);
+int vx_ipc_open(const char handle[64], void** base_out);
+int vx_ipc_close(void* base);
 
 /* ----------------------------------------------------------------------
  * The whole DeepSpeed-Ulysses layer behind one call, over an NCCL

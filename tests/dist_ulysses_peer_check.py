@@ -1,0 +1,70 @@
+"""Worker for test_ulysses_peer_two_gpus (run under torch.distributed.run):
+each rank feeds its chunk_by_rank share of a seeded global sequence through
+the peer-memory Ulysses layer and through the NCCL one; the two must agree
+bit for bit (same kernels on the same data), and rank 0 compares the
+gathered result with the oracle. Covers padded heads (H % P != 0), B = 2,
+a masked padded sequence and repeated calls on one workspace."""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import vidax_b200 as vx  # noqa: E402
+from vidax_b200 import _lib  # noqa: E402
+from vidax_b200.ulysses_peer import release_workspaces, sequence_parallel_self_attention_peer  # noqa: E402
+from oracle.attention_ref import compare, sdpa, seeded_qkv  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    vx.register_axis("sp", None)
+    ok = True
+    cases = [(1, 1024, 8, 128, None), (2, 768, 6, 128, None), (1, 512, 3, 128, None),
+             (1, 1024, 8, 64, 1000), (1, 1024, 8, 128, None)]   # last: the first shape again
+    for (B, S, H, D, valid) in cases:
+        q, k, v = seeded_qkv((B, S, H, D), 1700 + S + H + D)
+        sl = S // world
+        mine = [torch.from_numpy(np.ascontiguousarray(x[:, rank * sl:(rank + 1) * sl])).cuda().bfloat16()
+                for x in (q, k, v)]
+        for rep in range(2):
+            out = sequence_parallel_self_attention_peer(*mine, valid_len=valid)
+            ref = vx.sequence_parallel_self_attention(*mine, "sp", valid_len=valid)
+            torch.cuda.synchronize()
+            same = torch.equal(out, ref)
+            ok = ok and same
+            if not same:
+                print(f"rank {rank}: peer path differs from NCCL for B={B} S={S} H={H} D={D} "
+                      f"(rep {rep}): max {(out.float() - ref.float()).abs().max().item():.3g}",
+                      flush=True)
+        status = _lib.device_status(clear=True)
+        ok = ok and status == 0
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out.contiguous())
+        if rank == 0:
+            got = torch.cat(gathered, dim=1).float().cpu().numpy()
+            ref_np = sdpa(q, k, v, kv_len=np.full(B, valid)) if valid else sdpa(q, k, v)
+            mx, mean = compare(got, ref_np)
+            print(f"B={B} S={S} H={H} D={D} valid={valid}: max {mx:.3g} mean {mean:.3g} "
+                  f"status {status}", flush=True)
+            ok = ok and mx <= 2e-2 and mean <= 2e-3
+    flag = torch.tensor([1 if ok else 0], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    release_workspaces()
+    dist.destroy_process_group()
+    if rank == 0:
+        print("PEER OK" if flag.item() == 1 else "PEER FAILED", flush=True)
+    sys.exit(0 if flag.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()

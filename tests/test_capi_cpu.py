@@ -200,3 +200,39 @@ def test_ulysses_layer_workspace_size_without_device(lib):
     assert f(ctypes.byref(a), 8, ctypes.byref(n)) == 0
     assert n.value == 256 + 8 * (-(-(8 * 9450 * 2 * 128 * 2) // 256) * 256)
     assert f(ctypes.byref(a), 0, ctypes.byref(n)) != 0
+
+
+def test_peer_exchange_validation_without_device(lib):
+    """The peer forms of the slab kernels, the flag barrier and the IPC
+    helpers reject bad arguments before touching a device."""
+    from vidax_b200.ulysses_peer import PeerBarrierArgs, PeerSlabArgs
+    f = lib.vx_ulysses_pack_peers
+    f.argtypes = [ctypes.POINTER(PeerSlabArgs), ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    a = PeerSlabArgs()
+    a.slab.num_tensors, a.slab.seq, a.slab.heads, a.slab.head_dim = 1, 16, 16, 128
+    a.slab.src[0] = 4096
+    a.slab.stride[0][0], a.slab.stride[0][1] = 16 * 128, 128
+    a.slab.groups = 9
+    assert f(ctypes.byref(a), None) == 2            # more than 8 groups: VX_EUNSUPPORTED
+    a.slab.groups = 2
+    assert f(ctypes.byref(a), None) == 1            # peer addresses missing: VX_EINVAL
+    a.peer[0][0], a.peer[0][1] = 4096, 4104         # second one not 16-byte aligned
+    assert f(ctypes.byref(a), None) == 1
+    a.peer[0][1] = 8192
+    a.max_ctas = -1
+    assert f(ctypes.byref(a), None) == 1
+    b = lib.vx_peer_barrier
+    b.argtypes = [ctypes.POINTER(PeerBarrierArgs), ctypes.c_void_p]
+    b.restype = ctypes.c_int
+    ba = PeerBarrierArgs()
+    ba.world, ba.rank = 9, 0
+    assert b(ctypes.byref(ba), None) == 1
+    ba.world, ba.rank = 2, 2
+    assert b(ctypes.byref(ba), None) == 1
+    ba.rank = 0
+    assert b(ctypes.byref(ba), None) == 1           # NULL flag arrays
+    g = lib.vx_ipc_get_handle
+    g.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
+    g.restype = ctypes.c_int
+    assert g(None, ctypes.create_string_buffer(64), ctypes.byref(ctypes.c_int64())) == 1

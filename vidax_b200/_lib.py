@@ -44,6 +44,12 @@ EXPORTED_SYMBOLS = (
     "vx_ulysses_workspace_size",
     "vx_ulysses_attn_fwd",
     "vx_ulysses_attn_fwd_static",
+    "vx_ulysses_pack_peers",
+    "vx_ulysses_unpack_peers",
+    "vx_peer_barrier",
+    "vx_ipc_get_handle",
+    "vx_ipc_open",
+    "vx_ipc_close",
 )
 
 

@@ -21,7 +21,7 @@ LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libvidax_cuda.so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["vidax_cuda.cu", "ulysses_layer.cu"]
+SOURCES = ["vidax_cuda.cu", "ulysses_layer.cu", "peer_exchange.cu"]
 
 
 def nvcc_path() -> str:

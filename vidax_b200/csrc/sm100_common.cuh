@@ -23,6 +23,7 @@ enum DeviceStatus : int {
   kDevTimeoutSoftmax = 4,   // softmax waited too long for S / O
   kDevTimeoutDrain = 8,     // drain of in-flight async work timed out
   kDevSelfTest = 16,        // the wait-timeout self-test expired (expected)
+  kDevTimeoutPeer = 32,     // a cross-GPU flag barrier waited too long for a rank
 };
 
 // ~4 s at 2 GHz. A legitimate wait inside these kernels lasts microseconds.

@@ -21,12 +21,22 @@
 //
 // Both are pure 16-byte vector copies (HBM-bound); up to three tensors
 // (q, k, v) move in one launch.
+//
+// Peer forms (kPeer): the exchange itself, done by these kernels' stores and
+// loads over NVLink into / from the other ranks' memory (mapped into this
+// process by CUDA IPC), so the pack and the all-to-all are one pass:
+//   pack:   group g's chunk goes straight to peer[t][g], the slot rank g
+//           keeps for this rank's chunk in its receive slab;
+//   unpack: group g's chunk is read straight from peer[t][g], the slot of
+//           this rank's tokens in rank g's attention output.
 #pragma once
 
 #include "sm100_common.cuh"
 
 namespace vx {
 namespace ulysses {
+
+constexpr int kMaxPeerGroups = 8;  // one NVLink / NVSwitch domain
 
 struct PackParams {
   const uint4* src[3];
@@ -42,19 +52,22 @@ struct PackParams {
   int group_stride;  // strided-side heads between consecutive groups
   int head_offset;   // strided head of group 0's first packed head
   int group_valid;   // packed heads per group that map to real heads
+  uint4* peer[3][kMaxPeerGroups];  // kPeer: per group, the packed chunk's remote address
 };
 
 // grid = (x: chunks of the (s, hg, d) plane of one group, y: group, z: tensor).
 // Each thread moves one 16-byte vector; one integer division per vector.
-template <bool kPack>
+template <bool kPack, bool kPeer = false>
 __global__ void __launch_bounds__(256) head_slab_kernel(const __grid_constant__ PackParams p) {
   const int t = blockIdx.z;
   const int g = blockIdx.y;
   const int row_vecs = p.hg << p.vpd_log2;  // vectors per packed (g, s) row
   const long long plane = static_cast<long long>(p.seq) * row_vecs;
-  const long long packed_base = static_cast<long long>(g) * plane;
-  const uint4* __restrict__ src = p.src[t];
-  uint4* __restrict__ dst = p.dst[t];
+  // the packed chunk of group g: this rank's slab (offset g * plane) or, in
+  // the peer forms, its remote slot (offset 0 from the peer address)
+  const long long packed_base = kPeer ? 0 : static_cast<long long>(g) * plane;
+  const uint4* __restrict__ src = (kPeer && !kPack) ? p.peer[t][g] : p.src[t];
+  uint4* __restrict__ dst = (kPeer && kPack) ? p.peer[t][g] : p.dst[t];
   const long long ss = p.s_stride[t], hs = p.h_stride[t];
   const int dmask = (1 << p.vpd_log2) - 1;
   for (long long idx = blockIdx.x * 256LL + threadIdx.x; idx < plane;

@@ -165,6 +165,13 @@ int prepare_kernel(const void* fn, int dev, size_t smem) {
 
 }  // namespace
 
+int vx_internal_status_word(int** out) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != VX_OK) return rc;
+  return status_word(dev, out);
+}
+
 extern "C" {
 
 int vx_version(void) { return kVersion; }
@@ -282,8 +289,13 @@ int vx_attn_fwd(const vx_attn_args* a, vx_stream_t stream) {
 }
 
 
-static int head_slab(const vx_head_slab_args* a, vx_stream_t stream, bool pack) {
+// Checks a head-slab request and fills the kernel parameters. `src_at` /
+// `dst_at` say whether src[t] / dst[t] must be given (the peer forms take
+// one side from per-group peer addresses instead). Sets *empty for seq = 0.
+static int slab_params(const vx_head_slab_args* a, bool src_at, bool dst_at,
+                       vx::ulysses::PackParams* p, bool* empty) {
   using namespace vx::ulysses;
+  *empty = false;
   if (a == nullptr) return fail(VX_EINVAL, "args is NULL");
   if (a->num_tensors < 1 || a->num_tensors > 3)
     return fail(VX_EINVAL, "num_tensors must be 1..3 (got %d)", a->num_tensors);
@@ -292,44 +304,51 @@ static int head_slab(const vx_head_slab_args* a, vx_stream_t stream, bool pack) 
   if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
     return fail(VX_EUNSUPPORTED, "head_dim %d (64, 128 or 256)", a->head_dim);
   if (a->groups > 65535) return fail(VX_EUNSUPPORTED, "groups must be <= 65535");
-  if (a->seq == 0) return VX_OK;
-  PackParams p;
+  if (a->seq == 0) {
+    *empty = true;
+    return VX_OK;
+  }
+  *p = PackParams{};
   const int vpd = a->head_dim / 8;
-  p.vpd_log2 = vpd == 8 ? 3 : (vpd == 16 ? 4 : 5);
-  p.num_tensors = a->num_tensors;
-  p.seq = a->seq;
-  p.heads = a->heads;
-  p.groups = a->groups;
+  p->vpd_log2 = vpd == 8 ? 3 : (vpd == 16 ? 4 : 5);
+  p->num_tensors = a->num_tensors;
+  p->seq = a->seq;
+  p->heads = a->heads;
+  p->groups = a->groups;
   const int whole = (a->heads + a->groups - 1) / a->groups;
   const bool sub = a->slab_heads != 0 || a->group_stride != 0 || a->head_offset != 0 ||
                    a->group_valid != 0;
-  p.hg = sub ? a->slab_heads : whole;
-  p.group_stride = sub ? a->group_stride : whole;
-  p.head_offset = sub ? a->head_offset : 0;
-  p.group_valid = sub ? a->group_valid : whole;
-  if (p.hg <= 0 || p.group_stride < 0 || p.head_offset < 0 || p.group_valid < 0 ||
-      p.group_valid > p.hg)
+  p->hg = sub ? a->slab_heads : whole;
+  p->group_stride = sub ? a->group_stride : whole;
+  p->head_offset = sub ? a->head_offset : 0;
+  p->group_valid = sub ? a->group_valid : whole;
+  if (p->hg <= 0 || p->group_stride < 0 || p->head_offset < 0 || p->group_valid < 0 ||
+      p->group_valid > p->hg)
     return fail(VX_EINVAL, "bad sub-group selection (slab_heads %d, group_stride %d, "
                 "head_offset %d, group_valid %d)", a->slab_heads, a->group_stride,
                 a->head_offset, a->group_valid);
-  for (int t = 0; t < 3; ++t) {
-    p.src[t] = nullptr;
-    p.dst[t] = nullptr;
-    p.s_stride[t] = p.h_stride[t] = 0;
-  }
   for (int t = 0; t < a->num_tensors; ++t) {
-    if (a->src[t] == nullptr || a->dst[t] == nullptr)
+    if ((src_at && a->src[t] == nullptr) || (dst_at && a->dst[t] == nullptr))
       return fail(VX_EINVAL, "tensor %d: NULL pointer", t);
-    if (!aligned16(a->src[t]) || !aligned16(a->dst[t]))
+    if ((src_at && !aligned16(a->src[t])) || (dst_at && !aligned16(a->dst[t])))
       return fail(VX_EINVAL, "tensor %d: pointers must be 16-byte aligned", t);
     if (a->stride[t][0] % 8 != 0 || a->stride[t][1] % 8 != 0 || a->stride[t][0] < 0 ||
         a->stride[t][1] < 0)
       return fail(VX_EINVAL, "tensor %d: strides must be non-negative multiples of 8 elements", t);
-    p.src[t] = static_cast<const uint4*>(a->src[t]);
-    p.dst[t] = static_cast<uint4*>(a->dst[t]);
-    p.s_stride[t] = a->stride[t][0] / 8;
-    p.h_stride[t] = a->stride[t][1] / 8;
+    p->src[t] = src_at ? static_cast<const uint4*>(a->src[t]) : nullptr;
+    p->dst[t] = dst_at ? static_cast<uint4*>(a->dst[t]) : nullptr;
+    p->s_stride[t] = a->stride[t][0] / 8;
+    p->h_stride[t] = a->stride[t][1] / 8;
   }
+  return VX_OK;
+}
+
+static int head_slab(const vx_head_slab_args* a, vx_stream_t stream, bool pack) {
+  using namespace vx::ulysses;
+  PackParams p;
+  bool empty = false;
+  int rc = slab_params(a, true, true, &p, &empty);
+  if (rc != VX_OK || empty) return rc;
   const long long plane = static_cast<long long>(a->seq) * (p.hg << p.vpd_log2);
   long long bx = (plane + 255) / 256;
   if (bx > 4096) bx = 4096;
@@ -344,7 +363,51 @@ static int head_slab(const vx_head_slab_args* a, vx_stream_t stream, bool pack) 
   return VX_OK;
 }
 
+// Peer forms: pack writes group g's chunk to peer[t][g]; unpack reads it
+// from there. The strided side is this rank's own tensor.
+static int head_slab_peers(const vx_peer_slab_args* a, vx_stream_t stream, bool pack) {
+  using namespace vx::ulysses;
+  if (a == nullptr) return fail(VX_EINVAL, "args is NULL");
+  PackParams p;
+  bool empty = false;
+  int rc = slab_params(&a->slab, pack, !pack, &p, &empty);
+  if (rc != VX_OK || empty) return rc;
+  if (a->slab.groups > kMaxPeerGroups)
+    return fail(VX_EUNSUPPORTED, "peer forms take at most %d groups (got %d)", kMaxPeerGroups,
+                a->slab.groups);
+  if (a->max_ctas < 0) return fail(VX_EINVAL, "max_ctas must be >= 0");
+  for (int t = 0; t < a->slab.num_tensors; ++t)
+    for (int g = 0; g < a->slab.groups; ++g) {
+      if (a->peer[t][g] == nullptr || !aligned16(a->peer[t][g]))
+        return fail(VX_EINVAL, "tensor %d group %d: peer address NULL or not 16-byte aligned", t, g);
+      p.peer[t][g] = static_cast<uint4*>(a->peer[t][g]);
+    }
+  const long long plane = static_cast<long long>(a->slab.seq) * (p.hg << p.vpd_log2);
+  long long bx = (plane + 255) / 256;
+  if (bx > 4096) bx = 4096;
+  if (a->max_ctas > 0) {
+    const long long per = a->max_ctas / (static_cast<long long>(a->slab.groups) * a->slab.num_tensors);
+    bx = std::max(1LL, std::min(bx, per));
+  }
+  dim3 grid(static_cast<unsigned>(bx), a->slab.groups, a->slab.num_tensors);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (pack)
+    head_slab_kernel<true, true><<<grid, 256, 0, st>>>(p);
+  else
+    head_slab_kernel<false, true><<<grid, 256, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return cuda_fail(e, pack ? "ulysses pack-to-peers launch" : "ulysses unpack-from-peers launch");
+  return VX_OK;
+}
+
 int vx_ulysses_pack(const vx_head_slab_args* a, vx_stream_t stream) { return head_slab(a, stream, true); }
+int vx_ulysses_pack_peers(const vx_peer_slab_args* a, vx_stream_t stream) {
+  return head_slab_peers(a, stream, true);
+}
+int vx_ulysses_unpack_peers(const vx_peer_slab_args* a, vx_stream_t stream) {
+  return head_slab_peers(a, stream, false);
+}
 int vx_ulysses_unpack(const vx_head_slab_args* a, vx_stream_t stream) {
   return head_slab(a, stream, false);
 }

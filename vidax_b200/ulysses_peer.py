@@ -1,0 +1,333 @@
+"""DeepSpeed-Ulysses with the exchanges done by the slab kernels over NVLink.
+
+`sequence_parallel_self_attention` (vidax_b200.ulysses) moves the packed
+head slabs with NCCL all-to-alls. Here the ranks of one NVLink / NVSwitch
+domain map each other's workspace (CUDA IPC, once per process group) and
+the exchange becomes part of the slab kernels
+(src/vidax/core/attention.py:379-381 and :388):
+
+* tokens -> heads: `vx_ulysses_pack_peers` stores group g's chunk of this
+  rank's q / k / v straight into rank g's receive slab (SM stores over
+  NVLink; the pack and the all-to-all are one pass);
+* attention: the local kernel reads the receive slab and writes its output
+  into this rank's output slab, both in its own memory;
+* heads -> tokens: `vx_ulysses_unpack_peers` loads this rank's tokens of
+  every rank's output slab straight into the strided output rows (the
+  all-to-all and the unpack are one pass).
+
+`vx_peer_barrier` (flags in the ranks' workspaces, bounded waits) orders
+the steps across GPUs: after each slice's pack (its receive slabs are
+complete everywhere), after each slice's attention (the output slabs are),
+and at the end of each batch item (the workspace may be reused). The head
+group is processed in the same pipelined slices as the NCCL path: slice
+j+1's pack (on a side stream, with a small CTA budget) and slice j-1's
+unpack (on another) run beside the kernel on slice j, whose dynamic
+schedule leaves them SMs. Only ranks whose GPUs can reach each other's
+memory (one node) can use it; results are identical to the NCCL path's.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .ulysses import HeadSlabArgs, _pieces, _side_stream, _timed_attention
+
+MAX_GROUPS = 8
+CH_IN, CH_OUT, CH_END = 0, 1, 2   # flag arrays: one sequence of barriers each
+SLICE_CTAS = 0                    # CTA budget of a pack / unpack beside the kernel (0: none; measured best)
+PIPELINED = True                  # head slices pipelined against the kernel (else one slice)
+BARRIER_TIMEOUT_NS = 2_000_000_000
+
+
+class PeerSlabArgs(ctypes.Structure):
+    _fields_ = [
+        ("slab", HeadSlabArgs),
+        ("peer", (ctypes.c_void_p * MAX_GROUPS) * 3),
+        ("max_ctas", ctypes.c_int32),
+    ]
+
+
+class PeerBarrierArgs(ctypes.Structure):
+    _fields_ = [
+        ("flags", ctypes.c_void_p * MAX_GROUPS),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("epoch", ctypes.c_uint32),
+        ("timeout_ns", ctypes.c_int64),
+    ]
+
+
+def _fn(name, argtypes):
+    f = getattr(_lib.load(), name)
+    f.argtypes = argtypes
+    f.restype = ctypes.c_int
+    return f
+
+
+def ipc_handle(ptr: int) -> Tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding ptr, ptr's offset in it)."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_int64(0)
+    _lib.check(_fn("vx_ipc_get_handle", [ctypes.c_void_p, ctypes.c_char_p,
+                                         ctypes.POINTER(ctypes.c_int64)])(
+        ctypes.c_void_p(ptr), buf, ctypes.byref(off)))
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    base = ctypes.c_void_p()
+    _lib.check(_fn("vx_ipc_open", [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)])(
+        handle, ctypes.byref(base)))
+    return base.value
+
+
+def ipc_close(base: int) -> None:
+    _lib.check(_fn("vx_ipc_close", [ctypes.c_void_p])(ctypes.c_void_p(base)))
+
+
+def peer_barrier(flags: List[int], rank: int, epoch: int, stream,
+                 timeout_ns: int = BARRIER_TIMEOUT_NS) -> None:
+    """vx_peer_barrier over the flag arrays `flags` (one address per rank)."""
+    a = PeerBarrierArgs()
+    for g, f in enumerate(flags):
+        a.flags[g] = f
+    a.rank, a.world, a.epoch, a.timeout_ns = rank, len(flags), epoch, timeout_ns
+    _lib.check(_fn("vx_peer_barrier", [ctypes.POINTER(PeerBarrierArgs), ctypes.c_void_p])(
+        ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)))
+
+
+def slab_peers(pack: bool, strided, peers, heads: int, groups: int, sub, stream,
+               max_ctas: int = 0) -> None:
+    """vx_ulysses_pack_peers (pack) / vx_ulysses_unpack_peers: `strided` are
+    this rank's (S_loc, H, D) views, peers[t][g] the remote chunk addresses."""
+    a = PeerSlabArgs()
+    s = a.slab
+    s.num_tensors = len(strided)
+    seq, _, d = strided[0].shape
+    for t, x in enumerate(strided):
+        if x.stride(-1) != 1 or x.dtype != torch.bfloat16:
+            raise ValueError("bf16 views with head_dim contiguous")
+        if pack:
+            s.src[t] = x.data_ptr()
+        else:
+            s.dst[t] = x.data_ptr()
+        s.stride[t][0], s.stride[t][1] = x.stride(0), x.stride(1)
+        for g in range(groups):
+            a.peer[t][g] = peers[t][g]
+    s.seq, s.heads, s.head_dim, s.groups = seq, heads, d, groups
+    s.slab_heads, s.group_stride, s.head_offset, s.group_valid = sub
+    a.max_ctas = max_ctas
+    name = "vx_ulysses_pack_peers" if pack else "vx_ulysses_unpack_peers"
+    _lib.check(_fn(name, [ctypes.POINTER(PeerSlabArgs), ctypes.c_void_p])(
+        ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)))
+
+
+class PeerWorkspace:
+    """One rank's receive slabs (q, k, v), output slab and barrier flags,
+    with every rank's copy mapped into this process (collective: every rank
+    of `group` constructs it with the same sizes, on its own GPU)."""
+
+    def __init__(self, group, seq_local: int, heads: int, head_dim: int, device):
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.P > MAX_GROUPS:
+            raise NotImplementedError(f"the peer exchange spans at most {MAX_GROUPS} GPUs")
+        self.seq_local, self.heads, self.head_dim = seq_local, heads, head_dim
+        self.Hg = -(-heads // self.P)
+        elems = self.P * seq_local * self.Hg * head_dim
+        self.slab_bytes = (elems * 2 + 255) // 256 * 256
+        self.flag_off = 4 * self.slab_bytes
+        self.device = torch.device(device)
+        self.buf = torch.empty(self.flag_off + 256, dtype=torch.uint8, device=self.device)
+        self.buf[self.flag_off:].zero_()
+        torch.cuda.synchronize(self.device)
+        info = ipc_handle(self.buf.data_ptr())
+        infos: List = [None] * self.P
+        dist.all_gather_object(infos, info, group=group)
+        self._opened: List[int] = []
+        self.base: List[int] = []
+        for g, (handle, off) in enumerate(infos):
+            if g == self.rank:
+                self.base.append(self.buf.data_ptr())
+            else:
+                b = ipc_open(handle)
+                self._opened.append(b)
+                self.base.append(b + off)
+        self.epoch = [0, 0, 0]
+        # every rank has zeroed its flags and mapped the others' before any barrier
+        dist.barrier(group=group)
+
+    def fits(self, seq_local: int, heads: int, head_dim: int) -> bool:
+        return (seq_local, heads, head_dim) == (self.seq_local, self.heads, self.head_dim)
+
+    def slice_off(self, off: int) -> int:
+        """byte offset of a slice (first head `off` of the group) in a slab"""
+        return 2 * self.P * self.seq_local * off * self.head_dim
+
+    def local_view(self, slab: int, off: int, hs: int) -> torch.Tensor:
+        """(1, S, hs, D) view of this rank's slab `slab` (0-2 q/k/v received, 3 output)."""
+        start = slab * self.slab_bytes + self.slice_off(off)
+        n = self.P * self.seq_local * hs * self.head_dim
+        return self.buf[start:start + 2 * n].view(torch.bfloat16).view(
+            1, self.P * self.seq_local, hs, self.head_dim)
+
+    def remote(self, g: int, slab: int, off: int, hs: int) -> int:
+        """address of this rank's chunk of slice (off, hs) in rank g's slab"""
+        chunk = 2 * self.seq_local * hs * self.head_dim
+        return self.base[g] + slab * self.slab_bytes + self.slice_off(off) + self.rank * chunk
+
+    def barrier(self, channel: int, stream) -> None:
+        self.epoch[channel] += 1
+        flags = [b + self.flag_off + channel * MAX_GROUPS * 4 for b in self.base]
+        peer_barrier(flags, self.rank, self.epoch[channel] & 0xFFFFFFFF, stream)
+
+    def close(self) -> None:
+        """Collective: unmaps the other ranks' workspaces once all are done."""
+        if self.buf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for b in self._opened:
+            ipc_close(b)
+        self._opened = []
+        self.buf = None
+
+
+_WORKSPACES: Dict[Tuple[int, int], PeerWorkspace] = {}
+
+
+def workspace(group, seq_local: int, heads: int, head_dim: int, device) -> PeerWorkspace:
+    """The cached workspace of `group` on `device`, (re)made collectively when
+    the shapes change."""
+    key = (id(group), torch.device(device).index)
+    ws = _WORKSPACES.get(key)
+    if ws is not None and not ws.fits(seq_local, heads, head_dim):
+        ws.close()
+        ws = None
+    if ws is None:
+        ws = PeerWorkspace(group, seq_local, heads, head_dim, device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def release_workspaces() -> None:
+    """Collective: closes every cached workspace (before destroy_process_group)."""
+    for ws in _WORKSPACES.values():
+        ws.close()
+    _WORKSPACES.clear()
+
+
+def _ret_stream(device):
+    dev = torch.device(device).index
+    s = _RET_STREAMS.get(dev)
+    if s is None:
+        s = torch.cuda.Stream(device=dev)
+        _RET_STREAMS[dev] = s
+    return s
+
+
+_RET_STREAMS: Dict[int, "torch.cuda.Stream"] = {}
+
+
+def sequence_parallel_self_attention_peer(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group=None,
+    scale: Optional[float] = None, *, valid_len: Optional[int] = None,
+) -> torch.Tensor:
+    """sequence_parallel_self_attention (attention.py:341-388) with the
+    exchanges over peer memory: q, k, v (B, L_local, H, D) bf16, this rank's
+    token chunk; returns (B, L_local, H, D). `group`: a process group whose
+    ranks are GPUs of one NVLink domain (default: the default group)."""
+    group = group if group is not None else dist.distributed_c10d._get_default_group()
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError("self-attention needs q, k, v of equal shape")
+    B, S_loc, H, D = q.shape
+    ws = workspace(group, S_loc, H, D, q.device)
+    P, r, Hg = ws.P, ws.rank, ws.Hg
+    S = P * S_loc
+    sm_scale = D ** -0.5 if scale is None else scale
+    kv_len = None
+    if valid_len is not None and valid_len < S:
+        kv_len = torch.full((1,), valid_len, dtype=torch.int32, device=q.device)
+    sizes = _pieces(Hg) if PIPELINED else [Hg]
+    offs = [sum(sizes[:j]) for j in range(len(sizes))]
+    n = len(sizes)
+    out = torch.empty_like(q)
+    comp = torch.cuda.current_stream(q.device)
+    side = _side_stream(q.device)
+    ret = _ret_stream(q.device)
+    for b in range(B):
+        side.wait_stream(comp)
+        ret.wait_stream(comp)
+        ev_in = []
+        with torch.cuda.stream(side):
+            for j, (hs, off) in enumerate(zip(sizes, offs)):
+                peers = [[ws.remote(g, t, off, hs) for g in range(P)] for t in range(3)]
+                slab_peers(True, [q[b], k[b], v[b]], peers, H, P, (hs, Hg, off, hs), side,
+                           0 if j == 0 else SLICE_CTAS)
+                ws.barrier(CH_IN, side)
+                ev = torch.cuda.Event()
+                ev.record(side)
+                ev_in.append(ev)
+        for j, (hs, off) in enumerate(zip(sizes, offs)):
+            comp.wait_event(ev_in[j])
+            rq, rk, rv = (ws.local_view(t, off, hs) for t in range(3))
+            _timed_attention(rq, rk, rv, sm_scale, kv_len, ws.local_view(3, off, hs))
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            with torch.cuda.stream(ret):
+                ret.wait_event(ev)
+                ws.barrier(CH_OUT, ret)
+                peers = [[ws.remote(g, 3, off, hs) for g in range(P)]]
+                slab_peers(False, [out[b]], peers, H, P, (hs, Hg, off, hs), ret,
+                           0 if j == n - 1 else SLICE_CTAS)
+        comp.wait_stream(ret)
+        ws.barrier(CH_END, comp)
+    return out
+
+
+def launches_per_layer(heads: int, world: int, batch: int = 1) -> int:
+    """Kernel launches of one sequence_parallel_self_attention_peer call: per
+    batch item and head slice a pack, a barrier, the attention kernel, a
+    barrier and an unpack, and one closing barrier."""
+    n = len(_pieces(-(-heads // world))) if PIPELINED else 1
+    return batch * (5 * n + 1)
+
+
+def measure_exchange(x: torch.Tensor, reps: int = 10, group=None) -> dict:
+    """One q-sized tokens->heads exchange of the peer path on its own: the
+    pack-to-peers of x's whole head group (x: this rank's (S_loc, H, D)) and
+    its barrier, timed `reps` times after 3 warm-up runs (device time, max
+    over ranks). Uses the layer's cached workspace (call the layer first)."""
+    group = group if group is not None else dist.distributed_c10d._get_default_group()
+    S_loc, H, D = x.shape
+    ws = workspace(group, S_loc, H, D, x.device)
+    P, Hg = ws.P, ws.Hg
+    peers = [[ws.remote(g, 0, 0, Hg) for g in range(P)]]
+    stream = torch.cuda.current_stream(x.device)
+
+    def once():
+        slab_peers(True, [x], peers, H, P, (Hg, Hg, 0, Hg), stream)
+        ws.barrier(CH_IN, stream)
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize(x.device)
+    dist.barrier(group=group)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        once()
+    e1.record(stream)
+    torch.cuda.synchronize(x.device)
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=x.device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    ms = float(t.item())
+    cross = S_loc * Hg * D * 2 * (P - 1)   # bytes this rank sends to the others
+    return {"buffer_bytes_per_gpu": P * S_loc * Hg * D * 2, "bytes_per_gpu_per_direction": cross,
+            "ms": round(ms, 4), "gbs_per_direction": round(cross / ms / 1e6, 1),
+            "what": "pack-to-peers kernel + flag barrier (SM stores over NVLink)"}
