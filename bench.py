@@ -8,8 +8,11 @@ Workload (every N): the Ulysses self-attention layer of Wan2.1-14B at
 720p/81 frames -- B=1, S=75600 tokens, H=40 heads, head_dim 128, bf16, scale
 1/sqrt(128) -- with the sequence sharded evenly over the N ranks (strong
 scaling: total work fixed). At N=1 the layer is one local attention call; at
-N>1 it is pack -> NCCL all-to-all (tokens->heads) -> attention on H/N heads
-over the full sequence -> all-to-all back -> unpack. Inputs are seeded N(0,1)
+N>1 it is the tokens->heads exchange -> attention on H/N heads over the full
+sequence -> the heads->tokens exchange, pipelined by head slices, the
+exchanges done by the pack / unpack kernels storing into / loading from the
+other ranks' slabs over NVLink (`--exchange peer`, default) or as pack ->
+NCCL all-to-all -> unpack (`--exchange nccl`). Inputs are seeded N(0,1)
 synthetic tensors (no dataset exists for this path); every input exceeds the
 126 MB L2, so no flush is needed between steps.
 
@@ -819,9 +822,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
-                    help="N > 1: the Ulysses all-to-alls over NCCL, or done by the slab "
-                         "kernels over NVLink peer memory (vidax_b200.ulysses_peer)")
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="peer",
+                    help="N > 1: the Ulysses all-to-alls done by the slab kernels over "
+                         "NVLink peer memory (vidax_b200.ulysses_peer; default, 3.5-5 %% "
+                         "faster at N = 2 and 4), or over NCCL")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the extra cfg2 / cfg4 single-kernel measurements")
     ap.add_argument("--no-dit", action="store_true",
