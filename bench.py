@@ -522,10 +522,13 @@ def run_dit(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(dev)
     _lib.load()
     if world > 1:
-        vx.register_axis("sp", None)
+        vx.register_axis("sp", None, exchange=args.exchange)
     rec = dit_measure(world, dev, batch=1, steps=args.steps, warmup=args.warmup)
     if world > 1:
         vx.unregister_axis("sp")
+        if args.exchange == "peer":
+            from vidax_b200 import ulysses_peer
+            ulysses_peer.release_workspaces()   # collective, every rank
     if rank == 0:
         print(json.dumps({
             "metric": "Wan2.1-1.3B DiT forward step (cfg5), matmul TFLOP/s", "value": rec["tflops"],
@@ -589,7 +592,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(dev)
     _lib.load()
     if world > 1:
-        vx.register_axis("sp", None)
+        vx.register_axis("sp", None, exchange=args.exchange)
     if S_GLOBAL % world != 0:
         raise SystemExit(f"S={S_GLOBAL} does not split evenly over {world} ranks")
     s_loc = S_GLOBAL // world
@@ -611,9 +614,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             e1.record()
             ulysses_events.append((e0, e1))
             return o
-        if args.exchange == "peer":
-            return ulysses_peer.sequence_parallel_self_attention_peer(qq, kk, vv)
-        return vx.sequence_parallel_self_attention(qq, kk, vv, "sp")
+        return vx.sequence_parallel_self_attention(qq, kk, vv, "sp")   # exchange: the axis's
 
     def barrier():
         if world > 1:

@@ -57,6 +57,29 @@ def main():
             print(f"B={B} S={S} H={H} D={D} valid={valid}: max {mx:.3g} mean {mean:.3g} "
                   f"status {status}", flush=True)
             ok = ok and mx <= 2e-2 and mean <= 2e-3
+    # Wan's attend (fused norm + RoPE, then the layer) with the axis in peer
+    # mode against the same call in NCCL mode: B = 2, 12 heads (padded when
+    # they do not divide the ranks), this rank's tokens' RoPE rows
+    from vidax_b200.prologue import rope3d_freqs
+    B, T, Hh, W, heads, D = 2, 4, 8, 16, 12, 128
+    L = T * Hh * W
+    sl = L // world
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1750)
+    x = [torch.randn((B, L, heads * D), generator=gen, device="cuda").bfloat16() for _ in range(3)]
+    nq, nk = (1.0 + 0.1 * torch.randn(heads * D, generator=gen, device="cuda") for _ in range(2))
+    cos, sin = rope3d_freqs(T, Hh, W, D, device="cuda")
+    mine = [t[:, rank * sl:(rank + 1) * sl].contiguous() for t in x]
+    rope = (cos[rank * sl:(rank + 1) * sl].contiguous(), sin[rank * sl:(rank + 1) * sl].contiguous())
+    outs = {}
+    for mode in ("peer", "nccl"):
+        vx.register_axis("sp", None, exchange=mode)
+        outs[mode] = vx.attend(*mine, heads, norm_q=nq, norm_k=nk, rope=rope, sp_axis_name="sp")
+    torch.cuda.synchronize()
+    same = torch.equal(outs["peer"], outs["nccl"])
+    ok = ok and same and _lib.device_status(clear=True) == 0
+    print(f"rank {rank}: attend peer == nccl: {same}", flush=True)
+    vx.register_axis("sp", None)
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     release_workspaces()

@@ -224,3 +224,18 @@ def test_bench_parity_sample_over_ranks():
         errs.append(errq.get())
     assert not errs, errs
     assert all(p.exitcode == 0 for p in procs)
+
+
+def test_axis_exchange_mode():
+    """register_axis records how the Ulysses layers on the axis exchange
+    (NCCL all-to-alls by default, or the peer-memory slab kernels)."""
+    import pytest
+    from vidax_b200 import ulysses
+    ulysses.register_axis("xchg_test", None)
+    assert ulysses._exchange("xchg_test") == "nccl"
+    ulysses.register_axis("xchg_test", None, exchange="peer")
+    assert ulysses._exchange("xchg_test") == "peer"
+    with pytest.raises(ValueError):
+        ulysses.register_axis("xchg_test", None, exchange="mpi")
+    ulysses.unregister_axis("xchg_test")
+    assert ulysses._exchange("xchg_test") == "nccl"

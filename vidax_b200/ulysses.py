@@ -48,6 +48,7 @@ from . import _lib
 from .attention import flash_attention
 
 _AXES: Dict[str, Optional["dist.ProcessGroup"]] = {}
+_EXCHANGE: Dict[str, str] = {}
 _AXES_LOCK = threading.Lock()
 
 #: When set to a list, (start, end) CUDA events bracketing every attention
@@ -56,16 +57,28 @@ _AXES_LOCK = threading.Lock()
 KERNEL_EVENTS: Optional[list] = None
 
 
-def register_axis(name: str, group=None) -> None:
+def register_axis(name: str, group=None, exchange: str = "nccl") -> None:
     """Binds mesh axis `name` to a torch.distributed process group (None =
-    the default world group)."""
+    the default world group). `exchange` selects how the Ulysses layers on
+    this axis move the head slabs: "nccl" (all-to-alls; any topology) or
+    "peer" (the pack / unpack kernels store into / load from the other
+    ranks' slabs over NVLink, vidax_b200.ulysses_peer; ranks of one node)."""
+    if exchange not in ("nccl", "peer"):
+        raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
     with _AXES_LOCK:
         _AXES[name] = group
+        _EXCHANGE[name] = exchange
 
 
 def unregister_axis(name: str) -> None:
     with _AXES_LOCK:
         _AXES.pop(name, None)
+        _EXCHANGE.pop(name, None)
+
+
+def _exchange(name: str) -> str:
+    with _AXES_LOCK:
+        return _EXCHANGE.get(name, "nccl")
 
 
 def _group(name: str):
@@ -408,6 +421,10 @@ def sequence_parallel_self_attention(
     sm_scale = head_dim ** -0.5 if scale is None else scale
     if not (q.shape == k.shape == v.shape):
         raise ValueError("self-attention needs q, k, v of equal shape")
+    if _exchange(sp_axis_name) == "peer":
+        from .ulysses_peer import sequence_parallel_self_attention_peer
+        g = group if group is not None else dist.distributed_c10d._get_default_group()
+        return sequence_parallel_self_attention_peer(q, k, v, g, sm_scale, valid_len=valid_len)
     out = torch.empty_like(q)
     for b in range(q.shape[0]):
         _ulysses_one(q[b], k[b], v[b], out[b], group, P, sm_scale, valid_len)
@@ -424,6 +441,17 @@ def _attend_sp(q, k, v, num_heads, norm_q, norm_k, rope, eps, sp_axis_name, scal
     B, L, dim = q.shape
     H = num_heads
     D = dim // H
+    if _exchange(sp_axis_name) == "peer":
+        # norm + RoPE in natural (B, L, H, D) rows (the same HBM traffic as
+        # the NCCL path: there NCCL reads the packed slabs, here the pack
+        # kernel reads these rows and stores them into the peers' slabs)
+        from .ulysses_peer import sequence_parallel_self_attention_peer
+        rows = norm_rope_pack([q, k, v], H, norm_weights=[norm_q, norm_k, None], eps=eps,
+                              rope=rope, rope_mask=0b011 if rope is not None else 0)
+        qh, kh, vh = (r.view(B, L, H, D) for r in rows)
+        g = group if group is not None else dist.distributed_c10d._get_default_group()
+        out = sequence_parallel_self_attention_peer(qh, kh, vh, g, scale)
+        return out.reshape(B, L, dim)
     sizes = _pieces(-(-H // P))
     bufs = norm_rope_pack([q, k, v], H, norm_weights=[norm_q, norm_k, None], eps=eps,
                           rope=rope, rope_mask=0b011 if rope is not None else 0,
