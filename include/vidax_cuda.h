@@ -320,7 +320,9 @@ typedef struct vx_na3d_args {
   float scale;
   int32_t round_logits;
   int32_t q_box[3];    /* query tile box (t, h, w), product 128; all 0 = choose automatically */
-  int32_t pair_axis;   /* axis along which a CTA pairs two query boxes; ignored when q_box is 0 */
+  int32_t pair_axis;   /* 0-2: a CTA pairs two query boxes adjacent along t / h / w; 3: it
+                          pairs heads h and h + 1 of one box (head_dim 64 only); ignored when
+                          q_box is 0 (the library picks box and pairing by a time model) */
 } vx_na3d_args;
 
 int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);

@@ -156,6 +156,45 @@ def test_na3d_head_dim_64(shape, kernel):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("shape,kernel,q_box,kv_heads", [
+    ((1, 4, 9, 17, 2), (3, 5, 5), (2, 8, 8), 2),
+    ((1, 5, 12, 20, 3), (3, 7, 7), (1, 8, 16), 3),    # odd head count: the last pair has one head
+    ((2, 6, 10, 12, 4), (3, 5, 5), (4, 4, 8), 2),     # grouped K / V heads
+    ((1, 12, 13, 14, 2), (11, 11, 11), (8, 4, 4), 2),
+])
+def test_na3d_head_pairs_head_dim_64(shape, kernel, q_box, kv_heads):
+    """Head-pair tiling (pair_axis 3: the CTA's two query tiles are one box of
+    heads h and h + 1, each with its own K / V tiles) against the oracle and
+    against the box-pair tiling of the same box."""
+    import vidax_b200 as vx
+    B, T, H, W, NH = shape
+    q, _, _ = seeded_qkv((B, T, H, W, NH, 64), 760 + T * 7 + W, n=3)
+    _, k, v = seeded_qkv((B, T, H, W, kv_heads, 64), 761 + T * 7 + W, n=3)
+    q = to_bf16(q * np.float32(64 ** -0.5))
+    qd, kd, vd = _dev(q), _dev(k), _dev(v)
+    out = vx.neighborhood_attention_3d(qd, kd, vd, kernel, q_box=q_box, pair_axis=3)
+    boxes = vx.neighborhood_attention_3d(qd, kd, vd, kernel, q_box=q_box, pair_axis=0)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    rep = NH // kv_heads
+    ref = na3d(q, np.repeat(k, rep, axis=4), np.repeat(v, rep, axis=4), kernel)
+    mx, mean = compare(out.float().cpu().numpy(), ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+    mx2, _ = compare(out.float().cpu().numpy(), boxes.float().cpu().numpy())
+    assert mx2 <= MAX_ABS, mx2
+
+
+@pytest.mark.gpu
+def test_na3d_head_pairs_need_head_dim_64():
+    import vidax_b200 as vx
+    from vidax_b200._lib import VxError
+    q, k, v = seeded_qkv((1, 4, 8, 16, 2, 128), 79, n=3)
+    with pytest.raises(VxError):
+        vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (3, 5, 5), q_box=(2, 8, 8),
+                                     pair_axis=3)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("shape,kernel,world", [
     ((1, 21, 10, 24, 2), (5, 9, 9), 2),
     ((1, 21, 10, 24, 2), (5, 9, 9), 8),      # 2-3 frame slabs: halo from one neighbour

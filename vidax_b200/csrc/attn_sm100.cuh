@@ -46,20 +46,30 @@ constexpr uint32_t kHalfBytes = 128u * 64u * 2u;  // 128 rows x 64 cols: one 128
 constexpr float kRescaleThreshold = 8.0f;
 
 // Head-dimension dependent sizes (head_dim 64 or 128). A 128-row tile of
-// head_dim D is D/64 swizzle slabs of kHalfBytes.
-template <int HD>
+// head_dim D is D/64 swizzle slabs of kHalfBytes. A K / V stage holds KVT
+// tiles: one shared by both query tiles, or one per query tile when the two
+// query tiles belong to different heads (Geo::kKVTiles = 2).
+template <int HD, int KVT = 1>
 struct Dims {
   static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+  static_assert(KVT == 1 || KVT == 2, "one or two K / V tiles per stage");
   static constexpr int kHeadDim = HD;
   static constexpr int kHalves = HD / 64;
   static constexpr uint32_t kTileBytes = 128u * HD * 2u;
+  static constexpr uint32_t kKVStageBytes = KVT * kTileBytes;
   static constexpr uint32_t kSmemQ = 0;
   static constexpr uint32_t kSmemK = kSmemQ + 2 * kTileBytes;
-  static constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
-  static constexpr uint32_t kSmemBar = kSmemV + kStages * kTileBytes;
+  static constexpr uint32_t kSmemV = kSmemK + kStages * kKVStageBytes;
+  static constexpr uint32_t kSmemBar = kSmemV + kStages * kKVStageBytes;
   static constexpr uint32_t kSmemBytes = kSmemBar + 256 + 1024;  // + control block + alignment
   static constexpr uint32_t kTmemO = 256;                        // O_t at kTmemO + HD * t
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory per CTA");
 };
+// dynamic shared memory of attn_fwd_kernel<Geo, ...>
+template <class Geo>
+constexpr uint32_t smem_bytes() {
+  return Dims<Geo::kHeadDim, Geo::kKVTiles>::kSmemBytes;
+}
 
 // barrier slots
 enum : int {
@@ -140,9 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ typename Geo::Params p) {
-  using Dm = Dims<Geo::kHeadDim>;
+  using Dm = Dims<Geo::kHeadDim, Geo::kKVTiles>;
   constexpr int HD = Geo::kHeadDim;
   constexpr uint32_t kTileBytes = Dm::kTileBytes;
+  constexpr uint32_t kKVStage = Dm::kKVStageBytes;
   constexpr uint32_t kSmemQ = Dm::kSmemQ, kSmemK = Dm::kSmemK, kSmemV = Dm::kSmemV;
   constexpr uint32_t kSmemBar = Dm::kSmemBar;
   extern __shared__ uint8_t smem_dyn[];
@@ -255,9 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                mbar_wait(bar(kKEmpty + sk), ((g / kStages) & 1) ^ 1, abort_flag, status,
                          kDevTimeoutLoad);
           if (!ok) break;
-          mbar_expect_tx(bar(kQFull + 0), 2 * kTileBytes);
+          mbar_expect_tx(bar(kQFull + 0), kTileBytes + kKVStage);
           geo.load_q(&tm_q, 0, sbase + kSmemQ, bar(kQFull + 0), pol_q);
-          geo.load_kv(&tm_k, 0, sbase + kSmemK + sk * kTileBytes, bar(kQFull + 0), pol_kv);
+          geo.load_kv(&tm_k, 0, sbase + kSmemK + sk * kKVStage, bar(kQFull + 0), pol_kv);
           mbar_expect_tx(bar(kQFull + 1), kTileBytes);
           geo.load_q(&tm_q, 1, sbase + kSmemQ + kTileBytes, bar(kQFull + 1), pol_q);
           for (int j = 0; j < n; ++j) {
@@ -276,10 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
-            mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kTileBytes : kTileBytes);
-            geo.load_kv(&tm_v, j, sbase + kSmemV + s * kTileBytes, bar(kKVFull + s), pol_kv);
+            mbar_expect_tx(bar(kKVFull + s), has_next ? 2 * kKVStage : kKVStage);
+            geo.load_kv(&tm_v, j, sbase + kSmemV + s * kKVStage, bar(kKVFull + s), pol_kv);
             if (has_next)
-              geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kTileBytes, bar(kKVFull + s),
+              geo.load_kv(&tm_k, j + 1, sbase + kSmemK + s1 * kKVStage, bar(kKVFull + s),
                           pol_kv);
             last_pair = static_cast<int>(gj);
           }
@@ -328,8 +339,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       static_assert(kStages == 2, "descriptor selection below assumes two stages");
       const uint64_t k_desc0 = sdesc_sw128(sbase + kSmemK, 16, 1024);
       const uint64_t v_desc0 = sdesc_sw128(sbase + kSmemV, kHalfBytes, 1024);
-      // stage 1 = stage 0 + kTileBytes in the start-address field
-      constexpr uint64_t kStageStep = kTileBytes >> 4;
+      // stage 1 = stage 0 + kKVStage in the start-address field; with a K / V
+      // tile per query tile, query tile t's tile is t * kTileBytes further
+      constexpr uint64_t kStageStep = kKVStage >> 4;
+      auto kv_tile = [](int t) -> uint64_t {
+        return Geo::kKVTiles == 2 ? static_cast<uint64_t>(t) * (kTileBytes >> 4) : 0ull;
+      };
       uint32_t g = 0;
       int qi = 0;
       int p_count[2] = {0, 0};  // P publications consumed per query tile
@@ -351,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (geo.needs(t, 0)) {
-            issue_qk<HD>(tmem + 128 * t, q_desc[t], k_desc0 + ((g % kStages) ? kStageStep : 0));
+            issue_qk<HD>(tmem + 128 * t, q_desc[t],
+                         k_desc0 + ((g % kStages) ? kStageStep : 0) + kv_tile(t));
             tc_commit(bar(kSFull + t));
           }
         }
@@ -387,14 +403,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 0, !first_pv[t]);
-              issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d, 1, true);
+              issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d + kv_tile(t), 0,
+                                !first_pv[t]);
+              issue_pv_half<HD>(tmem + Dm::kTmemO + HD * t, tmem + 128 * t, v_d + kv_tile(t), 1,
+                                true);
               first_pv[t] = false;
               ++p_count[t];
               if (j == last[t]) tc_commit(bar(kOFull + t));
             }
             if (has_next && geo.needs(t, j + 1)) {
-              issue_qk<HD>(tmem + 128 * t, q_desc[t], k_next);
+              issue_qk<HD>(tmem + 128 * t, q_desc[t], k_next + kv_tile(t));
               tc_commit(bar(kSFull + t));
             }
           }
@@ -606,6 +624,7 @@ template <int HD>
 struct DenseGeo {
   static constexpr int kHeadDim = HD;
   static constexpr bool kPackedSoftmax = false;  // MUFU-bound: scalar arithmetic is as fast
+  static constexpr int kKVTiles = 1;             // both query tiles read the same K / V
   using Params = DenseParams;
   const DenseParams& p;
   int b, h, hk, q0, kv_valid;
@@ -741,15 +760,24 @@ __device__ __forceinline__ uint32_t bit_range(int lo, int hi, int n) {
   return upto_hi & ~upto_lo;
 }
 
-template <int KT, int KH, int KW, int HD>
+// kHP (head pair): the CTA's two query tiles are one query box of heads h
+// and h + 1 instead of two adjacent boxes of one head. Their key unions are
+// the same, so every KV step keeps both softmax warpgroups busy (no step
+// where only one box needs the key tile), at the price of a K / V tile per
+// head in each stage (head_dim 64: 160 KB of shared memory).
+template <int KT, int KH, int KW, int HD, bool kHP = false>
 struct NaGeo {
   static constexpr int kHeadDim = HD;
   static constexpr bool kPackedSoftmax = true;  // issue-bound (masks): two columns per instruction
+  static constexpr int kKVTiles = kHP ? 2 : 1;
   static_assert(KT * KH * KW == 128, "key tile must hold 128 keys");
   static_assert(KW == 8 || KW == 16 || KW == 32, "key tile width 8, 16 or 32");
   using Params = NaParams;
   const NaParams& p;
   int b, head, head_kv;
+  int head_kv1;           // kHP: K / V head of query tile 1 (NHkv when that tile is empty)
+  bool tile1_valid;       // kHP: head + 1 < NH
+  int out_head;           // the softmax thread's query tile's head
   int org[2][3];          // query tile origins
   int lim[3];             // grid extents (T, H, W)
   int u0[3], n_ax[3];     // CTA key union start and tiles per axis
@@ -765,9 +793,19 @@ struct NaGeo {
   // Work unit u = (region, head, batch), region fastest.
   __device__ NaGeo(const NaParams& prm, int unit) : p(prm) {
     const int rest = unit / p.num_regions;
-    head = rest % p.NH;
-    b = rest / p.NH;
-    head_kv = head / (p.NH / p.NHkv);
+    if (kHP) {
+      const int pairs = (p.NH + 1) / 2;
+      head = 2 * (rest % pairs);
+      b = rest / pairs;
+    } else {
+      head = rest % p.NH;
+      b = rest / p.NH;
+    }
+    const int grp = p.NH / p.NHkv;
+    head_kv = head / grp;
+    tile1_valid = !kHP || head + 1 < p.NH;
+    head_kv1 = kHP ? (tile1_valid ? (head + 1) / grp : p.NHkv) : head_kv;
+    out_head = head;
     lim[0] = p.T_g;  // window clamping: the global grid
     lim[1] = p.H;
     lim[2] = p.W;
@@ -792,7 +830,8 @@ struct NaGeo {
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         const int a0 = org[t][a];
-        const int a1 = min(a0 + p.qbox[a], qlim[a]);
+        // kHP: an odd head count leaves the last pair's second tile empty
+        const int a1 = (t == 1 && !tile1_valid) ? a0 : min(a0 + p.qbox[a], qlim[a]);
         if (a0 < a1) {
           wu0[t][a] = na_start(a0 + qoff[a], lim[a], ksz[a]);
           wu1[t][a] = na_start(a1 - 1 + qoff[a], lim[a], ksz[a]) + ksz[a];
@@ -862,9 +901,10 @@ struct NaGeo {
   __device__ void load_q(const CUtensorMap* tm, int t, uint32_t dst, uint32_t bar,
                          uint64_t pol) const {
     const int bt = b * p.T + org[t][0];
+    const int hq = kHP ? head + t : head;  // an empty tile 1 reads the zero fill past NH
 #pragma unroll
     for (int c = 0; c < HD / 64; ++c)
-      tma_load_5d(dst + c * kHalfBytes, tm, bar, 64 * c, head, org[t][2], org[t][1], bt, pol);
+      tma_load_5d(dst + c * kHalfBytes, tm, bar, 64 * c, hq, org[t][2], org[t][1], bt, pol);
   }
   __device__ void load_kv(const CUtensorMap* tm, int j, uint32_t dst, uint32_t bar,
                           uint64_t pol) const {
@@ -874,6 +914,12 @@ struct NaGeo {
 #pragma unroll
     for (int c = 0; c < HD / 64; ++c)
       tma_load_5d(dst + c * kHalfBytes, tm, bar, 64 * c, head_kv, o[2], o[1], bt, pol);
+    if (kHP) {  // query tile 1's head: the stage's second tile
+      constexpr uint32_t kTile = 128u * HD * 2u;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c)
+        tma_load_5d(dst + kTile + c * kHalfBytes, tm, bar, 64 * c, head_kv1, o[2], o[1], bt, pol);
+    }
   }
   __device__ void softmax_setup(int t, int row) {
     const int qw = p.qbox[2], qh = p.qbox[1];
@@ -888,7 +934,8 @@ struct NaGeo {
     qc[0] = (t ? org[1][0] : org[0][0]) + it;
     qc[1] = (t ? org[1][1] : org[0][1]) + ih;
     qc[2] = (t ? org[1][2] : org[0][2]) + iw;
-    row_valid = qc[0] < p.T && qc[1] < p.H && qc[2] < p.W;
+    row_valid = qc[0] < p.T && qc[1] < p.H && qc[2] < p.W && (t == 0 || tile1_valid);
+    out_head = kHP ? head + t : head;
     const int ksz[3] = {p.kt, p.kh, p.kw};
     const int qg[3] = {min(qc[0], p.T - 1) + p.q_t0, qc[1], qc[2]};  // global query coordinates
 #pragma unroll
@@ -994,7 +1041,7 @@ struct NaGeo {
   }
   __device__ __nv_bfloat16* row_ptr() const {
     return p.o + b * p.o_sb + qc[0] * p.o_st + qc[1] * p.o_sh + qc[2] * p.o_sw +
-           head * p.o_shead;
+           out_head * p.o_shead;
   }
   // A warp's 32 rows are 32 different output rows (neighbouring w are a whole
   // token apart), so each store touches 32 lines: 32-byte stores write whole

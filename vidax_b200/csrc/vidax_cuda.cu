@@ -439,6 +439,9 @@ __global__ void selftest_wait_kernel(int* status, long long limit, int* result) 
 constexpr int kNaKT = 2, kNaKH = 4, kNaKW = 16;
 template <int HD>
 using NaGeoDefault = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW, HD>;
+// query tiles = one box of two heads (head_dim 64 only: a K / V tile per head
+// in each stage)
+using NaGeoHeadPair64 = vx::attn::NaGeo<kNaKT, kNaKH, kNaKW, 64, true>;
 
 int na_start_host(int i, int L, int k) { return std::min(std::max(i - k / 2, 0), L - k); }
 
@@ -510,7 +513,30 @@ double na_tiling_cost(const int lim[3], const int ksz[3], const int qbox[3], int
          w_unit * static_cast<double>(units);
 }
 
-struct NaChoice { int qbox[3]; int pair; };
+struct NaChoice { int qbox[3]; int pair; };  // pair 3: the two tiles are heads h, h + 1
+
+// Predicted run time per head of the head-pair tiling with query box `qbox`:
+// every key tile of one box's window union is a paired step (both heads'
+// tiles need it), and a unit (one box, two heads) pays the unit cost once.
+double na_tiling_cost_heads(const int lim[3], const int ksz[3], const int qbox[3], int head_dim) {
+  const double w_paired = head_dim == 128 ? 18.0 : 17.0;
+  const double w_unit = head_dim == 128 ? 111.0 : 27.1;
+  const int kvb[3] = {kNaKT, kNaKH, kNaKW};
+  int regions[3];
+  for (int a = 0; a < 3; ++a) regions[a] = (lim[a] + qbox[a] - 1) / qbox[a];
+  // the union's tile count factorises over the axes
+  long long per_axis[3] = {0, 0, 0};
+  for (int a = 0; a < 3; ++a)
+    for (int r = 0; r < regions[a]; ++r) {
+      const int a0 = r * qbox[a], a1 = std::min(a0 + qbox[a], lim[a]);
+      const int lo = na_start_host(a0, lim[a], ksz[a]);
+      const int hi = na_start_host(a1 - 1, lim[a], ksz[a]) + ksz[a];
+      per_axis[a] += (hi - lo + kvb[a] - 1) / kvb[a];
+    }
+  const double tiles = static_cast<double>(per_axis[0]) * per_axis[1] * per_axis[2];
+  const double units = static_cast<double>(regions[0]) * regions[1] * regions[2];
+  return (w_paired * tiles + w_unit * units) / 2.0;  // one unit serves two heads
+}
 
 NaChoice na_choose_tiling(const int lim[3], const int ksz[3], int head_dim) {
   static std::mutex mu;
@@ -532,6 +558,14 @@ NaChoice na_choose_tiling(const int lim[3], const int ksz[3], int head_dim) {
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
         best = {{c[0], c[1], c[2]}, pair};
+      }
+    }
+  if (head_dim == 64)  // head pairs fit shared memory at head_dim 64 only
+    for (const auto& c : cands) {
+      const double cost = na_tiling_cost_heads(lim, ksz, c, head_dim);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = {{c[0], c[1], c[2]}, 3};
       }
     }
   std::lock_guard<std::mutex> lk(mu);
@@ -630,7 +664,10 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
       ch.qbox[i] = a->q_box[i];
     }
     if (ch.qbox[0] * ch.qbox[1] * ch.qbox[2] != 128) return fail(VX_EINVAL, "q_box must hold 128 queries");
-    if (a->pair_axis < 0 || a->pair_axis > 2) return fail(VX_EINVAL, "pair_axis must be 0, 1 or 2");
+    if (a->pair_axis < 0 || a->pair_axis > 3)
+      return fail(VX_EINVAL, "pair_axis must be 0, 1, 2 (box pairs) or 3 (head pairs)");
+    if (a->pair_axis == 3 && a->head_dim != 64)
+      return fail(VX_EUNSUPPORTED, "head pairs (pair_axis 3) need head_dim 64");
     ch.pair = a->pair_axis;
   }
 
@@ -676,6 +713,7 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
   p.kt = ksz[0];
   p.kh = ksz[1];
   p.kw = ksz[2];
+  const bool head_pair = ch.pair == 3;
   long long n_regions = 1;
   for (int i = 0; i < 3; ++i) {
     p.qbox[i] = ch.qbox[i];
@@ -683,11 +721,11 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
     p.regions[i] = (lim[i] + rsz - 1) / rsz;
     n_regions *= p.regions[i];
   }
-  const long long units = n_regions * a->heads * a->batch;
+  const long long units = n_regions * (head_pair ? (a->heads + 1) / 2 : a->heads) * a->batch;
   if (units > 0x7fffffffLL) return fail(VX_EUNSUPPORTED, "grid too large");
   p.num_regions = static_cast<int>(n_regions);
   p.num_units = static_cast<int>(units);
-  p.pair_axis = ch.pair;
+  p.pair_axis = head_pair ? -1 : ch.pair;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.round_logits = a->round_logits ? 1 : 0;
 
@@ -701,6 +739,11 @@ static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_strea
     if (HD == 128) {
       auto kern = attn_fwd_kernel<NaGeoDefault<128>, kSchedSteal>;
       constexpr uint32_t smem = Dims<128>::kSmemBytes;
+      if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
+      kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
+    } else if (head_pair) {
+      auto kern = attn_fwd_kernel<NaGeoHeadPair64, kSchedSteal>;
+      constexpr uint32_t smem = smem_bytes<NaGeoHeadPair64>();
       if ((rc = prepare_kernel(reinterpret_cast<const void*>(kern), dev, smem)) != VX_OK) return rc;
       kern<<<grid, kThreads, smem, st>>>(tq, tk, tv, p);
     } else {

@@ -83,7 +83,9 @@ def neighborhood_attention_3d(
     Returns (B, T, H, W, NH, HD). `scale` multiplies q.k (vidax pre-scales q,
     hence 1.0). `round_logits=True` rounds each q.k to bf16 before the fp32
     softmax, as the reference's bf16 einsum does (diffusion_vae.py:222).
-    `q_box` / `pair_axis` override the kernel's query tiling (tuning only).
+    `q_box` / `pair_axis` override the kernel's query tiling (tuning only;
+    pair_axis 0-2 pairs two boxes adjacent along t / h / w, 3 pairs two heads
+    of one box at head_dim 64).
     """
     return _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, None)
 
