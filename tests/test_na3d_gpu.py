@@ -231,6 +231,32 @@ def test_na3d_time_slabs_emulated_ranks(shape, kernel, world):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("shape,kernel,world", [((1, 9, 10, 20, 3), (3, 5, 5), 3),
+                                               ((1, 8, 12, 16, 2), (3, 7, 7), 4)])
+def test_na3d_time_slabs_head_dim_64(shape, kernel, world):
+    """Time slabs at head_dim 64, where the tiling chooser picks head pairs:
+    the slabs assembled along T equal the unsharded oracle."""
+    import vidax_b200 as vx
+    from vidax_b200.na_parallel import key_ranges, slab_bounds, split_sizes
+    B, T, H, W, NH = shape
+    q, k, v = seeded_qkv((B, T, H, W, NH, 64), 930 + T + W + world, n=3)
+    q = to_bf16(q * np.float32(64 ** -0.5))
+    qd, kd, vd = _dev(q), _dev(k), _dev(v)
+    bounds = slab_bounds(split_sizes(T, world))
+    outs = []
+    for r, (kv0, kv1) in enumerate(key_ranges(bounds, kernel[0])):
+        b0, b1 = bounds[r], bounds[r + 1]
+        outs.append(vx.neighborhood_attention_3d_slab(
+            qd[:, b0:b1].contiguous(), kd[:, kv0:kv1].contiguous(), vd[:, kv0:kv1].contiguous(),
+            kernel, t_global=T, q_t0=b0, kv_t0=kv0))
+    got = torch.cat(outs, dim=1)
+    torch.cuda.synchronize()
+    assert _status_clean()
+    mx, mean = compare(got.float().cpu().numpy(), na3d(q, k, v, kernel))
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.gpu
 def test_na3d_slab_rejects_uncovered_windows():
     import vidax_b200 as vx
     from vidax_b200._lib import VxInvalid
