@@ -523,7 +523,16 @@ def run_dit(args, rank: int, world: int, local_rank: int):
     _lib.load()
     if world > 1:
         vx.register_axis("sp", None, exchange=args.exchange)
-    rec = dit_measure(world, dev, batch=1, steps=args.steps, warmup=args.warmup)
+    try:
+        rec = dit_measure(world, dev, batch=1, steps=args.steps, warmup=args.warmup)
+    except Exception as e:   # the peer mapping failed on every rank alike: NCCL instead
+        from vidax_b200.ulysses_peer import PeerUnavailable
+        if not isinstance(e, PeerUnavailable):
+            raise
+        print(f"peer exchange unavailable, NCCL used: {e}", file=sys.stderr, flush=True)
+        args.exchange = "nccl"
+        vx.register_axis("sp", None, exchange="nccl")
+        rec = dit_measure(world, dev, batch=1, steps=args.steps, warmup=args.warmup)
     if world > 1:
         vx.unregister_axis("sp")
         if args.exchange == "peer":
@@ -627,6 +636,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    exchange_note = None
+    if world > 1 and args.exchange == "peer":
+        try:
+            layer(q, k, v)   # the first call maps the ranks' workspaces (collective)
+        except ulysses_peer.PeerUnavailable as e:   # raised on every rank alike
+            exchange_note = f"peer exchange unavailable, NCCL used: {e}"
+            print(exchange_note, file=sys.stderr, flush=True)
+            args.exchange = "nccl"
+            vx.register_axis("sp", None, exchange="nccl")
     for _ in range(args.warmup):
         layer(q, k, v)
     torch.cuda.synchronize()
@@ -783,6 +801,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": S_GLOBAL, "heads": H,
                    "head_dim": D, "parallelism": f"ulysses-sp{world}" if world > 1 else "single",
                    "exchange": (args.exchange if world > 1 else None),
+                   **({"exchange_note": exchange_note} if exchange_note else {}),
                    "l2": "inputs larger than L2 (774 MB per tensor), no flush"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 4),

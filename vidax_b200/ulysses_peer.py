@@ -43,6 +43,11 @@ PIPELINED = True                  # head slices pipelined against the kernel (el
 BARRIER_TIMEOUT_NS = 2_000_000_000
 
 
+class PeerUnavailable(RuntimeError):
+    """The ranks of the group cannot map each other's memory (raised on every
+    rank alike, so the caller can switch the axis to the NCCL exchange)."""
+
+
 class PeerSlabArgs(ctypes.Structure):
     _fields_ = [
         ("slab", HeadSlabArgs),
@@ -146,18 +151,38 @@ class PeerWorkspace:
         self.buf = torch.empty(self.flag_off + 256, dtype=torch.uint8, device=self.device)
         self.buf[self.flag_off:].zero_()
         torch.cuda.synchronize(self.device)
-        info = ipc_handle(self.buf.data_ptr())
+        why = ""
+        try:
+            info = ipc_handle(self.buf.data_ptr())
+        except _lib.VxError as e:   # e.g. an allocator without cudaMalloc'd segments
+            info, why = None, str(e)
         infos: List = [None] * self.P
         dist.all_gather_object(infos, info, group=group)
         self._opened: List[int] = []
         self.base: List[int] = []
-        for g, (handle, off) in enumerate(infos):
-            if g == self.rank:
-                self.base.append(self.buf.data_ptr())
-            else:
-                b = ipc_open(handle)
+        if all(i is not None for i in infos):
+            for g, (handle, off) in enumerate(infos):
+                if g == self.rank:
+                    self.base.append(self.buf.data_ptr())
+                    continue
+                try:
+                    b = ipc_open(handle)
+                except _lib.VxError as e:   # no peer access between these GPUs
+                    why = str(e)
+                    break
                 self._opened.append(b)
                 self.base.append(b + off)
+        else:
+            why = why or "another rank could not export its workspace"
+        # every rank learns whether all of them mapped all the others
+        ok = torch.tensor([0 if why else 1], device=self.device, dtype=torch.int32)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if ok.item() == 0:
+            for b in self._opened:
+                ipc_close(b)
+            self._opened, self.buf = [], None
+            raise PeerUnavailable("the peer-memory exchange cannot map the ranks' memory "
+                                  f"({why or 'failed on another rank'}); use exchange='nccl'")
         self.epoch = [0, 0, 0]
         # every rank has zeroed its flags and mapped the others' before any barrier
         dist.barrier(group=group)
