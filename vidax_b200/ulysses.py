@@ -306,6 +306,12 @@ def sequence_parallel_self_attention_from_host(
     slice j+1 and downloads of slice j-1 run on copy streams while the kernel
     computes slice j."""
     from .hostio import _check_host, _side_streams, check_host_out, group_sizes
+    if _exchange(sp_axis_name) == "peer":
+        from .ulysses_peer import sequence_parallel_self_attention_from_host_peer
+        g = _group(sp_axis_name)
+        g = g if g is not None else dist.distributed_c10d._get_default_group()
+        return sequence_parallel_self_attention_from_host_peer(q, k, v, g, scale, out=out,
+                                                               device=device)
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check_host(name, t)
     if not (q.shape == k.shape == v.shape):

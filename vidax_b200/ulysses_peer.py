@@ -149,7 +149,9 @@ class PeerWorkspace:
         self.flag_off = 4 * self.slab_bytes
         self.device = torch.device(device)
         self.buf = torch.empty(self.flag_off + 256, dtype=torch.uint8, device=self.device)
-        self.buf[self.flag_off:].zero_()
+        # zeroed once: the flags, and the padded heads (H % P != 0) the
+        # host-buffer form never writes (the slab kernels write them as zeros)
+        self.buf.zero_()
         torch.cuda.synchronize(self.device)
         why = ""
         try:
@@ -356,3 +358,75 @@ def measure_exchange(x: torch.Tensor, reps: int = 10, group=None) -> dict:
     return {"buffer_bytes_per_gpu": P * S_loc * Hg * D * 2, "bytes_per_gpu_per_direction": cross,
             "ms": round(ms, 4), "gbs_per_direction": round(cross / ms / 1e6, 1),
             "what": "pack-to-peers kernel + flag barrier (SM stores over NVLink)"}
+
+
+def sequence_parallel_self_attention_from_host_peer(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group=None,
+    scale: Optional[float] = None, *, out: Optional[torch.Tensor] = None,
+    device: Optional[torch.device] = None,
+) -> torch.Tensor:
+    """The host-buffer form (pinned q, k, v (B, L_local, H, D) in, pinned
+    output back; complete once the current stream is synchronised) with the
+    exchanges over peer memory: per slice, one 2-D copy per rank group moves
+    that group's heads of every local token from host rows straight into
+    rank g's receive slab, and after every rank's kernel one 2-D copy per
+    group moves this rank's tokens of rank g's output slab straight into
+    the host output rows -- the copies are the all-to-alls. Uploads of slice
+    j+1 and downloads of slice j-1 run on copy streams beside the kernel on
+    slice j; flag barriers order them across GPUs."""
+    from .hostio import _check_host, _side_streams, check_host_out, group_sizes
+    from .ulysses import _rows_copy, _slab_heads
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_host(name, t)
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError("self-attention needs q, k, v of equal shape")
+    if out is not None:
+        check_host_out(out, q.shape)
+    group = group if group is not None else dist.distributed_c10d._get_default_group()
+    B, S_loc, H, D = q.shape
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    sm_scale = D ** -0.5 if scale is None else scale
+    if out is None:
+        out = torch.empty((B, S_loc, H, D), dtype=torch.bfloat16).pin_memory()
+    ws = workspace(group, S_loc, H, D, device)
+    P, Hg = ws.P, ws.Hg
+    sizes = group_sizes(Hg, 8)
+    offs = [sum(sizes[:j]) for j in range(len(sizes))]
+    es = 2
+    comp = torch.cuda.current_stream(device)
+    h2d, d2h = _side_streams(device)
+    h2d.wait_stream(comp)
+    d2h.wait_stream(comp)
+    for b in range(B):
+        ready = []
+        for hs, off in zip(sizes, offs):
+            for t, src in enumerate((q, k, v)):
+                for g in range(P):
+                    h0, n = _slab_heads(g, Hg, off, hs, H)
+                    if n > 0:
+                        _rows_copy(ws.remote(g, t, off, hs), hs * D * es,
+                                   src.data_ptr() + (b * src.stride(0) + h0 * src.stride(2)) * es,
+                                   src.stride(1) * es, n * D * es, S_loc, h2d)
+            ws.barrier(CH_IN, h2d)   # every rank's uploads of this slice landed
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            ready.append(ev)
+        for j, (hs, off) in enumerate(zip(sizes, offs)):
+            comp.wait_event(ready[j])
+            rq, rk, rv = (ws.local_view(t, off, hs) for t in range(3))
+            _timed_attention(rq, rk, rv, sm_scale, None, ws.local_view(3, off, hs))
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            d2h.wait_event(ev)
+            ws.barrier(CH_OUT, d2h)  # every rank's kernel on this slice finished
+            for g in range(P):
+                h0, n = _slab_heads(g, Hg, off, hs, H)
+                if n > 0:
+                    _rows_copy(out.data_ptr() + (b * out.stride(0) + h0 * out.stride(2)) * es,
+                               out.stride(1) * es, ws.remote(g, 3, off, hs), hs * D * es,
+                               n * D * es, S_loc, d2h)
+        ws.barrier(CH_END, d2h)      # every rank's downloads done: the workspace is free
+        h2d.wait_stream(d2h)
+    comp.wait_stream(d2h)
+    return out
