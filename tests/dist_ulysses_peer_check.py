@@ -79,6 +79,23 @@ def main():
     same = torch.equal(outs["peer"], outs["nccl"])
     ok = ok and same and _lib.device_status(clear=True) == 0
     print(f"rank {rank}: attend peer == nccl: {same}", flush=True)
+    # joint [text; visual] layout (CogVideoX) in peer mode against NCCL mode
+    for (B, T_len, S, H) in [(1, 226, 1024, 8), (2, 77, 512, 6), (1, 64, 512, 3)]:
+        q, k, v = seeded_qkv((B, T_len + S, H, 128), 1950 + T_len + S + H)
+        sl = S // world
+
+        def local(x):
+            return np.concatenate([x[:, :T_len], x[:, T_len + rank * sl:T_len + (rank + 1) * sl]],
+                                  axis=1)
+        mine = [torch.from_numpy(np.ascontiguousarray(local(x))).cuda().bfloat16() for x in (q, k, v)]
+        res = {}
+        for mode in ("peer", "nccl"):
+            vx.register_axis("sp", None, exchange=mode)
+            res[mode] = vx.sequence_parallel_joint_self_attention(*mine, T_len, "sp")
+        torch.cuda.synchronize()
+        same = torch.equal(res["peer"], res["nccl"])
+        ok = ok and same and _lib.device_status(clear=True) == 0
+        print(f"rank {rank}: joint peer == nccl for B={B} T={T_len} S={S} H={H}: {same}", flush=True)
     # host-buffer form in peer mode: uploads straight into the peers' receive
     # slabs, downloads straight from their output slabs; equal to the device
     # form bit for bit (padded heads included)

@@ -485,6 +485,10 @@ def sequence_parallel_joint_self_attention(
     text output is all-gathered over heads.
     """
     group = _group(sp_axis_name)
+    if _exchange(sp_axis_name) == "peer":
+        from .ulysses_peer import sequence_parallel_joint_self_attention_peer
+        g = group if group is not None else dist.distributed_c10d._get_default_group()
+        return sequence_parallel_joint_self_attention_peer(q, k, v, text_len, g, scale)
     P = dist.get_world_size(group)
     r = dist.get_rank(group)
     B, L, H, D = q.shape

@@ -136,15 +136,17 @@ class PeerWorkspace:
     with every rank's copy mapped into this process (collective: every rank
     of `group` constructs it with the same sizes, on its own GPU)."""
 
-    def __init__(self, group, seq_local: int, heads: int, head_dim: int, device):
+    def __init__(self, group, seq_local: int, heads: int, head_dim: int, device,
+                 prefix: int = 0):
         self.group = group
+        self.prefix = prefix   # rows before the received chunks (the joint layout's text)
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if self.P > MAX_GROUPS:
             raise NotImplementedError(f"the peer exchange spans at most {MAX_GROUPS} GPUs")
         self.seq_local, self.heads, self.head_dim = seq_local, heads, head_dim
         self.Hg = -(-heads // self.P)
-        elems = self.P * seq_local * self.Hg * head_dim
+        elems = (prefix + self.P * seq_local) * self.Hg * head_dim
         self.slab_bytes = (elems * 2 + 255) // 256 * 256
         self.flag_off = 4 * self.slab_bytes
         self.device = torch.device(device)
@@ -189,24 +191,34 @@ class PeerWorkspace:
         # every rank has zeroed its flags and mapped the others' before any barrier
         dist.barrier(group=group)
 
-    def fits(self, seq_local: int, heads: int, head_dim: int) -> bool:
-        return (seq_local, heads, head_dim) == (self.seq_local, self.heads, self.head_dim)
+    def fits(self, seq_local: int, heads: int, head_dim: int, prefix: int = 0) -> bool:
+        return ((seq_local, heads, head_dim, prefix) ==
+                (self.seq_local, self.heads, self.head_dim, self.prefix))
+
+    def rows(self) -> int:
+        return self.prefix + self.P * self.seq_local
 
     def slice_off(self, off: int) -> int:
         """byte offset of a slice (first head `off` of the group) in a slab"""
-        return 2 * self.P * self.seq_local * off * self.head_dim
+        return 2 * self.rows() * off * self.head_dim
 
     def local_view(self, slab: int, off: int, hs: int) -> torch.Tensor:
-        """(1, S, hs, D) view of this rank's slab `slab` (0-2 q/k/v received, 3 output)."""
+        """(1, prefix + S, hs, D) view of this rank's slab `slab` (0-2 q/k/v
+        received, 3 output)."""
         start = slab * self.slab_bytes + self.slice_off(off)
-        n = self.P * self.seq_local * hs * self.head_dim
+        n = self.rows() * hs * self.head_dim
         return self.buf[start:start + 2 * n].view(torch.bfloat16).view(
-            1, self.P * self.seq_local, hs, self.head_dim)
+            1, self.rows(), hs, self.head_dim)
 
     def remote(self, g: int, slab: int, off: int, hs: int) -> int:
         """address of this rank's chunk of slice (off, hs) in rank g's slab"""
-        chunk = 2 * self.seq_local * hs * self.head_dim
-        return self.base[g] + slab * self.slab_bytes + self.slice_off(off) + self.rank * chunk
+        row = self.prefix + self.rank * self.seq_local
+        return (self.base[g] + slab * self.slab_bytes + self.slice_off(off) +
+                2 * row * hs * self.head_dim)
+
+    def remote_prefix(self, g: int, slab: int, off: int) -> int:
+        """address of the prefix rows of slice `off` in rank g's slab"""
+        return self.base[g] + slab * self.slab_bytes + self.slice_off(off)
 
     def barrier(self, channel: int, stream) -> None:
         self.epoch[channel] += 1
@@ -228,16 +240,17 @@ class PeerWorkspace:
 _WORKSPACES: Dict[Tuple[int, int], PeerWorkspace] = {}
 
 
-def workspace(group, seq_local: int, heads: int, head_dim: int, device) -> PeerWorkspace:
+def workspace(group, seq_local: int, heads: int, head_dim: int, device,
+              prefix: int = 0) -> PeerWorkspace:
     """The cached workspace of `group` on `device`, (re)made collectively when
     the shapes change."""
     key = (id(group), torch.device(device).index)
     ws = _WORKSPACES.get(key)
-    if ws is not None and not ws.fits(seq_local, heads, head_dim):
+    if ws is not None and not ws.fits(seq_local, heads, head_dim, prefix):
         ws.close()
         ws = None
     if ws is None:
-        ws = PeerWorkspace(group, seq_local, heads, head_dim, device)
+        ws = PeerWorkspace(group, seq_local, heads, head_dim, device, prefix)
         _WORKSPACES[key] = ws
     return ws
 
@@ -429,4 +442,53 @@ def sequence_parallel_self_attention_from_host_peer(
         ws.barrier(CH_END, d2h)      # every rank's downloads done: the workspace is free
         h2d.wait_stream(d2h)
     comp.wait_stream(d2h)
+    return out
+
+
+def sequence_parallel_joint_self_attention_peer(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, text_len: int, group=None,
+    scale: Optional[float] = None,
+) -> torch.Tensor:
+    """Joint [text; visual] Ulysses attention (attention.py:391-464) with the
+    exchanges over peer memory. q, k, v (B, text_len + L_vis_local, H, D):
+    the text prefix replicated on every rank, the visual rows this rank's
+    chunk. The text rows of this rank's head group are packed into its own
+    receive slab's prefix, the visual rows stored straight into every rank's
+    slab; after the joint kernel the visual output is loaded back from every
+    rank's output slab and the text output gathered over heads the same way
+    (the all_gather of attention.py:463 as loads of each rank's prefix rows)."""
+    from .ulysses import pack_heads
+    group = group if group is not None else dist.distributed_c10d._get_default_group()
+    if not (q.shape == k.shape == v.shape):
+        raise ValueError("self-attention needs q, k, v of equal shape")
+    B, L, H, D = q.shape
+    S_loc = L - text_len
+    ws = workspace(group, S_loc, H, D, q.device, prefix=text_len)
+    P, r, Hg = ws.P, ws.rank, ws.Hg
+    sm_scale = D ** -0.5 if scale is None else scale
+    h0 = r * Hg
+    nvalid = max(0, min(h0 + Hg, H) - h0)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(q.device)
+    sub = (Hg, Hg, 0, Hg)
+    for b in range(B):
+        # this rank's text heads -> its own slabs' prefix rows (zero heads past H)
+        for t, x in enumerate((q, k, v)):
+            prefix = ws.local_view(t, 0, Hg)[0, :text_len]
+            pack_heads([x[b, :text_len]], 1, out=[prefix.unsqueeze(0)],
+                       sub=(Hg, 0, h0, nvalid))
+        peers = [[ws.remote(g, t, 0, Hg) for g in range(P)] for t in range(3)]
+        slab_peers(True, [q[b, text_len:], k[b, text_len:], v[b, text_len:]], peers, H, P, sub,
+                   stream)
+        ws.barrier(CH_IN, stream)
+        rq, rk, rv = (ws.local_view(t, 0, Hg) for t in range(3))
+        _timed_attention(rq, rk, rv, sm_scale, None, ws.local_view(3, 0, Hg))
+        ws.barrier(CH_OUT, stream)
+        # visual rows: this rank's tokens of every rank's head group
+        slab_peers(False, [out[b, text_len:]], [[ws.remote(g, 3, 0, Hg) for g in range(P)]],
+                   H, P, sub, stream)
+        # text rows: every rank's head group of the text (the all_gather)
+        slab_peers(False, [out[b, :text_len]], [[ws.remote_prefix(g, 3, 0) for g in range(P)]],
+                   H, P, sub, stream)
+        ws.barrier(CH_END, stream)
     return out
