@@ -24,6 +24,13 @@ j+1's pack (on a side stream, with a small CTA budget) and slice j-1's
 unpack (on another) run beside the kernel on slice j, whose dynamic
 schedule leaves them SMs. Only ranks whose GPUs can reach each other's
 memory (one node) can use it; results are identical to the NCCL path's.
+
+The same workspace serves the host-buffer form (the 2-D host copies
+themselves land in the peers' receive slabs and leave from their output
+slabs) and the joint [text; visual] layer (the text rows in a prefix of the
+receive slab). `vidax_b200.ulysses` dispatches to these functions for an
+axis registered with exchange="peer". If the ranks cannot map each other's
+memory, the workspace raises PeerUnavailable on every rank alike.
 """
 from __future__ import annotations
 
