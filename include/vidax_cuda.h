@@ -323,6 +323,8 @@ typedef struct vx_na3d_args {
   int32_t pair_axis;   /* 0-2: a CTA pairs two query boxes adjacent along t / h / w; 3: it
                           pairs heads h and h + 1 of one box (head_dim 64 only); ignored when
                           q_box is 0 (the library picks box and pairing by a time model) */
+  int32_t kv_tile[3];  /* key tile box (t, h, w) with q_box: all 0 = (2, 4, 16); head pairs also
+                          take (4, 2, 16), (2, 8, 8) and (4, 4, 8) */
 } vx_na3d_args;
 
 int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);

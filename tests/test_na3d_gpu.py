@@ -156,13 +156,17 @@ def test_na3d_head_dim_64(shape, kernel):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape,kernel,q_box,kv_heads", [
-    ((1, 4, 9, 17, 2), (3, 5, 5), (2, 8, 8), 2),
-    ((1, 5, 12, 20, 3), (3, 7, 7), (1, 8, 16), 3),    # odd head count: the last pair has one head
-    ((2, 6, 10, 12, 4), (3, 5, 5), (4, 4, 8), 2),     # grouped K / V heads
-    ((1, 12, 13, 14, 2), (11, 11, 11), (8, 4, 4), 2),
+@pytest.mark.parametrize("shape,kernel,q_box,kv_heads,kv_tile", [
+    ((1, 4, 9, 17, 2), (3, 5, 5), (2, 8, 8), 2, (2, 4, 16)),
+    ((1, 5, 12, 20, 3), (3, 7, 7), (1, 8, 16), 3, (2, 4, 16)),  # odd head count: one head in the last pair
+    ((2, 6, 10, 12, 4), (3, 5, 5), (4, 4, 8), 2, (2, 4, 16)),   # grouped K / V heads
+    ((1, 12, 13, 14, 2), (11, 11, 11), (8, 4, 4), 2, (2, 4, 16)),
+    ((1, 5, 12, 20, 3), (3, 7, 7), (2, 8, 8), 3, (4, 2, 16)),   # the other key tiles
+    ((1, 6, 11, 19, 2), (3, 5, 5), (8, 4, 4), 2, (2, 8, 8)),
+    ((2, 6, 10, 12, 4), (3, 5, 5), (2, 16, 4), 2, (4, 4, 8)),
+    ((1, 9, 13, 14, 2), (11, 11, 11), (8, 4, 4), 1, (2, 8, 8)),
 ])
-def test_na3d_head_pairs_head_dim_64(shape, kernel, q_box, kv_heads):
+def test_na3d_head_pairs_head_dim_64(shape, kernel, q_box, kv_heads, kv_tile):
     """Head-pair tiling (pair_axis 3: the CTA's two query tiles are one box of
     heads h and h + 1, each with its own K / V tiles) against the oracle and
     against the box-pair tiling of the same box."""
@@ -172,7 +176,8 @@ def test_na3d_head_pairs_head_dim_64(shape, kernel, q_box, kv_heads):
     _, k, v = seeded_qkv((B, T, H, W, kv_heads, 64), 761 + T * 7 + W, n=3)
     q = to_bf16(q * np.float32(64 ** -0.5))
     qd, kd, vd = _dev(q), _dev(k), _dev(v)
-    out = vx.neighborhood_attention_3d(qd, kd, vd, kernel, q_box=q_box, pair_axis=3)
+    out = vx.neighborhood_attention_3d(qd, kd, vd, kernel, q_box=q_box, pair_axis=3,
+                                       kv_tile=kv_tile)
     boxes = vx.neighborhood_attention_3d(qd, kd, vd, kernel, q_box=q_box, pair_axis=0)
     torch.cuda.synchronize()
     assert _status_clean()
@@ -192,6 +197,13 @@ def test_na3d_head_pairs_need_head_dim_64():
     with pytest.raises(VxError):
         vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (3, 5, 5), q_box=(2, 8, 8),
                                      pair_axis=3)
+    q, k, v = seeded_qkv((1, 4, 8, 16, 2, 64), 80, n=3)
+    with pytest.raises(VxError):   # box pairs read (2, 4, 16) key tiles only
+        vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (3, 5, 5), q_box=(2, 8, 8),
+                                     pair_axis=0, kv_tile=(2, 8, 8))
+    with pytest.raises(VxError):   # not a key tile of the library
+        vx.neighborhood_attention_3d(_dev(q), _dev(k), _dev(v), (3, 5, 5), q_box=(2, 8, 8),
+                                     pair_axis=3, kv_tile=(1, 2, 64))
 
 
 @pytest.mark.gpu

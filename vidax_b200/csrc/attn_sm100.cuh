@@ -960,72 +960,37 @@ struct NaGeo {
     const uint32_t hmask = bit_range(ws[1] - o[1], ws[1] + p.kh - o[1], KH);
     const uint32_t wmask = bit_range(ws[2] - o[2], ws[2] + p.kw - o[2], KW);
     constexpr int kRowsPerChunk = 32 / KW;  // (ct, ch) rows of the tile per chunk (>= 1)
+    constexpr uint32_t kChunkRows = (1u << kRowsPerChunk) - 1u;
+    // factored: cm[0] = the w bits of one tile row, cm[1] bit r = tile row r
+    // (r = ct * KH + ch) lies in the window's t and h ranges
+    uint32_t rows = 0;
+#pragma unroll
+    for (int r = 0; r < KT * KH; ++r)
+      if (((tmask >> (r / KH)) & 1u) && ((hmask >> (r % KH)) & 1u)) rows |= 1u << r;
+    if (!row_valid || wmask == 0u) rows = 0;
+    cm[0] = wmask;
+    cm[1] = rows;
+    cm[2] = cm[3] = 0;
     uint32_t active = 0;
-    if constexpr (KW == 16) {
-      uint32_t rows = 0;
 #pragma unroll
-      for (int r = 0; r < KT * KH; ++r)
-        if (((tmask >> (r / KH)) & 1u) && ((hmask >> (r % KH)) & 1u)) rows |= 1u << r;
-      if (!row_valid || wmask == 0u) rows = 0;
-      cm[0] = wmask;
-      cm[1] = rows;
-      cm[2] = cm[3] = 0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (__any_sync(0xffffffffu, ((rows >> (2 * c)) & 3u) != 0u)) active |= 1u << c;
-    } else {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t m = 0;
-#pragma unroll
-      for (int rr = 0; rr < kRowsPerChunk; ++rr) {
-        const int tile_row = c * kRowsPerChunk + rr;  // = ct * KH + ch
-        const int ct = tile_row / KH, ch = tile_row % KH;
-        const bool on = ((tmask >> ct) & 1u) && ((hmask >> ch) & 1u);
-        if (on) m |= (KW == 32 ? wmask : (wmask << (rr * KW)));
-      }
-      if (!row_valid) m = 0;
-      cm[c] = m;
-      if (__any_sync(0xffffffffu, m != 0u)) active |= 1u << c;
-    }
-    }
+    for (int c = 0; c < 4; ++c)
+      if (__any_sync(0xffffffffu, ((rows >> (kRowsPerChunk * c)) & kChunkRows) != 0u))
+        active |= 1u << c;
     return active;
   }
   // Hidden columns of the active chunks become -inf (after the optional bf16
   // rounding of q.k); inactive chunks are left as they are.
+  // Adds the column bias (0 / -inf by the w bit) and the tile-row bias (0 /
+  // -inf by the row bit) to each score, two columns per f32x2 add.
   __device__ void apply_masks(const uint32_t (&cm)[4], uint32_t active,
                               uint32_t (&sr)[4][32]) const {
-    if constexpr (KW == 16) {
-      const float ninf = neg_inf();
-      uint64_t wb[8];  // column biases, two columns per register pair
+    constexpr int kRowsPerChunk = 32 / KW;
+    const float ninf = neg_inf();
+    uint64_t wb[KW / 2];  // column biases of one tile row, two columns per register pair
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        wb[k] = f2_pack(((cm[0] >> (2 * k)) & 1u) ? 0.f : ninf,
-                        ((cm[0] >> (2 * k + 1)) & 1u) ? 0.f : ninf);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (!((active >> c) & 1u)) continue;
-        if (p.round_logits) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            sr[c][i] = __float_as_uint(__bfloat162float(__float2bfloat16_rn(__uint_as_float(sr[c][i]))));
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const float rb = ((cm[1] >> (2 * c + r)) & 1u) ? 0.f : ninf;
-          const uint64_t rb2 = f2_pack(rb, rb);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int i = 16 * r + 2 * k;
-            float a, bq;
-            f2_unpack(f2_add(f2_add(f2_pack(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1])),
-                                    wb[k]), rb2), a, bq);
-            sr[c][i] = __float_as_uint(a);
-            sr[c][i + 1] = __float_as_uint(bq);
-          }
-        }
-      }
-    } else {
+    for (int k = 0; k < KW / 2; ++k)
+      wb[k] = f2_pack(((cm[0] >> (2 * k)) & 1u) ? 0.f : ninf,
+                      ((cm[0] >> (2 * k + 1)) & 1u) ? 0.f : ninf);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       if (!((active >> c) & 1u)) continue;
@@ -1035,8 +1000,19 @@ struct NaGeo {
           sr[c][i] = __float_as_uint(__bfloat162float(__float2bfloat16_rn(__uint_as_float(sr[c][i]))));
       }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sr[c][i] = ((cm[c] >> i) & 1u) ? sr[c][i] : 0xff800000u;
-    }
+      for (int r = 0; r < kRowsPerChunk; ++r) {
+        const float rb = ((cm[1] >> (kRowsPerChunk * c + r)) & 1u) ? 0.f : ninf;
+        const uint64_t rb2 = f2_pack(rb, rb);
+#pragma unroll
+        for (int k = 0; k < KW / 2; ++k) {
+          const int i = KW * r + 2 * k;
+          float a, bq;
+          f2_unpack(f2_add(f2_add(f2_pack(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1])),
+                                  wb[k]), rb2), a, bq);
+          sr[c][i] = __float_as_uint(a);
+          sr[c][i + 1] = __float_as_uint(bq);
+        }
+      }
     }
   }
   __device__ __nv_bfloat16* row_ptr() const {

@@ -42,6 +42,7 @@ class Na3dArgs(ctypes.Structure):
         ("round_logits", ctypes.c_int32),
         ("q_box", ctypes.c_int32 * 3),
         ("pair_axis", ctypes.c_int32),
+        ("kv_tile", ctypes.c_int32 * 3),
     ]
 
 
@@ -77,17 +78,19 @@ def neighborhood_attention_3d(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kernel_size: Sequence[int],
     *, scale: float = 1.0, round_logits: bool = False,
     q_box: Optional[Tuple[int, int, int]] = None, pair_axis: int = 0,
+    kv_tile: Optional[Tuple[int, int, int]] = None,
 ) -> torch.Tensor:
     """3-D neighborhood attention over (B, T, H, W, NH, HD) bf16 tensors.
 
     Returns (B, T, H, W, NH, HD). `scale` multiplies q.k (vidax pre-scales q,
     hence 1.0). `round_logits=True` rounds each q.k to bf16 before the fp32
     softmax, as the reference's bf16 einsum does (diffusion_vae.py:222).
-    `q_box` / `pair_axis` override the kernel's query tiling (tuning only;
-    pair_axis 0-2 pairs two boxes adjacent along t / h / w, 3 pairs two heads
-    of one box at head_dim 64).
+    `q_box` / `pair_axis` / `kv_tile` override the kernel's tiling (tuning
+    only; pair_axis 0-2 pairs two boxes adjacent along t / h / w, 3 pairs two
+    heads of one box at head_dim 64; kv_tile is the key tile box, (2, 4, 16)
+    unless head pairs take (4, 2, 16), (2, 8, 8) or (4, 4, 8)).
     """
-    return _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, None)
+    return _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, None, kv_tile)
 
 
 class Na3dSlab(ctypes.Structure):
@@ -113,7 +116,7 @@ def neighborhood_attention_3d_slab(
     return _na3d(q, k, v, kernel_size, scale, round_logits, None, 0, slab)
 
 
-def _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, slab):
+def _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, slab, kv_tile=None):
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check6(name, t)
     if not (q.device == k.device == v.device):
@@ -139,6 +142,8 @@ def _na3d(q, k, v, kernel_size, scale, round_logits, q_box, pair_axis, slab):
     if q_box is not None:
         a.q_box[0], a.q_box[1], a.q_box[2] = q_box
         a.pair_axis = pair_axis
+        if kv_tile is not None:
+            a.kv_tile[0], a.kv_tile[1], a.kv_tile[2] = kv_tile
     lib = _lib.load()
     with torch.cuda.device(q.device):
         s = torch.cuda.current_stream(q.device)
