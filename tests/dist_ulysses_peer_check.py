@@ -84,10 +84,11 @@ def main():
         q, k, v = seeded_qkv((B, T_len + S, H, 128), 1950 + T_len + S + H)
         sl = S // world
 
-        def local(x):
+        def rank_rows(x):
             return np.concatenate([x[:, :T_len], x[:, T_len + rank * sl:T_len + (rank + 1) * sl]],
                                   axis=1)
-        mine = [torch.from_numpy(np.ascontiguousarray(local(x))).cuda().bfloat16() for x in (q, k, v)]
+        mine = [torch.from_numpy(np.ascontiguousarray(rank_rows(x))).cuda().bfloat16()
+                for x in (q, k, v)]
         res = {}
         for mode in ("peer", "nccl"):
             vx.register_axis("sp", None, exchange=mode)
@@ -114,6 +115,22 @@ def main():
         print(f"rank {rank}: host path (peer) == device path for B={B} S={S} H={H}: {same}",
               flush=True)
     vx.register_axis("sp", None)
+    # a rank that never arrives: rank 0's barrier wait is bounded (50 ms
+    # here), expires, sets the status bit and returns; rank 1 stays alive
+    # and mapped meanwhile, then both close the workspace together
+    from vidax_b200.ulysses_peer import CH_END, MAX_GROUPS, PeerWorkspace, peer_barrier
+    ws = PeerWorkspace(dist.distributed_c10d._get_default_group(), 64, 2 * world, 64,
+                       torch.device("cuda", local))
+    _lib.device_status(clear=True)
+    if rank == 0:
+        flags = [b + ws.flag_off + CH_END * MAX_GROUPS * 4 for b in ws.base]
+        peer_barrier(flags, 0, 1, torch.cuda.current_stream(), timeout_ns=50_000_000)
+        torch.cuda.synchronize()
+        expired = bool(_lib.device_status(clear=True) & 32)
+        ok = ok and expired
+        print(f"rank 0: barrier without rank 1 expired and reported: {expired}", flush=True)
+    dist.barrier()
+    ws.close()
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     release_workspaces()
