@@ -329,6 +329,15 @@ typedef struct vx_na3d_args {
 
 int vx_na3d_fwd(const vx_na3d_args* args, vx_stream_t stream);
 
+/* The tiling vx_na3d_fwd picks for a T x H x W grid and window (q_box all 0):
+ * query box, pairing (0-2 box pairs along t / h / w, 3 head pairs) and key
+ * tile, from the library's time model. Host only (no device work); for
+ * inspection and tuning. No counterpart in the reference (its NA is one
+ * einsum over gathered windows). */
+int vx_na3d_tiling(int32_t T, int32_t H, int32_t W, int32_t kernel_t, int32_t kernel_h,
+                   int32_t kernel_w, int32_t head_dim, int32_t q_box_out[3], int32_t* pair_out,
+                   int32_t kv_tile_out[3]);
+
 /* Time-slab form of vx_na3d_fwd for sequence (T-axis) sharding: q and o hold
  * frames [q_t0, q_t0 + T) of a T_global-frame grid, k and v frames
  * [kv_t0, kv_t0 + T_kv) (the caller's own frames plus the halo received from

@@ -236,3 +236,26 @@ def test_peer_exchange_validation_without_device(lib):
     g.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
     g.restype = ctypes.c_int
     assert g(None, ctypes.create_string_buffer(64), ctypes.byref(ctypes.c_int64())) == 1
+
+
+def test_na3d_tiling_choices_without_device(lib):
+    """vx_na3d_tiling is host arithmetic (the kernel's time model). On these
+    shapes its picks were also the fastest of the tilings timed on a B200:
+    box pairs along h at head_dim 128 (cfg4), head pairs at head_dim 64 with
+    the key tile per window (LTX-2.5 decoder stages)."""
+    from vidax_b200.neighborhood import tiling
+    assert tiling((21, 30, 52), (5, 9, 9), 128) == {"q_box": (2, 8, 8), "pair": "h",
+                                                    "kv_tile": (2, 4, 16)}
+    assert tiling((32, 64, 96), (3, 5, 5), 64) == {"q_box": (2, 16, 4), "pair": "heads",
+                                                   "kv_tile": (4, 4, 8)}
+    assert tiling((16, 32, 48), (3, 7, 7), 64) == {"q_box": (2, 8, 8), "pair": "heads",
+                                                   "kv_tile": (4, 2, 16)}
+    assert tiling((32, 64, 96), (11, 11, 11), 64) == {"q_box": (8, 4, 4), "pair": "heads",
+                                                      "kv_tile": (2, 4, 16)}
+    # head_dim 128 never takes head pairs (their K / V stages do not fit)
+    assert tiling((32, 64, 96), (3, 5, 5), 128)["pair"] != "heads"
+    from vidax_b200._lib import VxError
+    with pytest.raises(VxError):
+        tiling((0, 4, 4), (3, 3, 3), 64)
+    with pytest.raises(VxError):
+        tiling((4, 4, 4), (3, 3, 3), 96)

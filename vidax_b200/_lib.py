@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "vx_na3d_fwd",
     "vx_na3d_fwd_slab",
     "vx_na3d_window_start",
+    "vx_na3d_tiling",
     "vx_ulysses_pack",
     "vx_ulysses_unpack",
     "vx_norm_rope_pack",

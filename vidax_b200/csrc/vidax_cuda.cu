@@ -629,6 +629,25 @@ int vx_na3d_window_start(int32_t length, int32_t kernel, int32_t* start_out) {
   return VX_OK;
 }
 
+int vx_na3d_tiling(int32_t T, int32_t H, int32_t W, int32_t kernel_t, int32_t kernel_h,
+                   int32_t kernel_w, int32_t head_dim, int32_t q_box_out[3], int32_t* pair_out,
+                   int32_t kv_tile_out[3]) {
+  if (T < 1 || H < 1 || W < 1 || kernel_t < 1 || kernel_h < 1 || kernel_w < 1)
+    return fail(VX_EINVAL, "grid and kernel sizes must be >= 1");
+  if (head_dim != 64 && head_dim != 128) return fail(VX_EUNSUPPORTED, "head_dim must be 64 or 128");
+  if (q_box_out == nullptr || pair_out == nullptr || kv_tile_out == nullptr)
+    return fail(VX_EINVAL, "NULL output");
+  const int lim[3] = {T, H, W};
+  const int ksz[3] = {std::min(kernel_t, T), std::min(kernel_h, H), std::min(kernel_w, W)};
+  const NaChoice ch = na_choose_tiling(lim, ksz, head_dim);
+  for (int i = 0; i < 3; ++i) {
+    q_box_out[i] = ch.qbox[i];
+    kv_tile_out[i] = ch.kv[i];
+  }
+  *pair_out = ch.pair;
+  return VX_OK;
+}
+
 static int na3d_launch(const vx_na3d_args* a, const vx_na3d_slab* slab, vx_stream_t stream);
 
 int vx_na3d_fwd(const vx_na3d_args* a, vx_stream_t stream) { return na3d_launch(a, nullptr, stream); }

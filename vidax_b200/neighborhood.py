@@ -46,6 +46,23 @@ class Na3dArgs(ctypes.Structure):
     ]
 
 
+def tiling(grid: Sequence[int], kernel_size: Sequence[int], head_dim: int) -> dict:
+    """The tiling the kernel picks for a (T, H, W) grid and window: query
+    box, pairing ("t" / "h" / "w" box pairs or "heads") and key tile."""
+    qb = (ctypes.c_int32 * 3)()
+    kv = (ctypes.c_int32 * 3)()
+    pair = ctypes.c_int32(0)
+    fn = _lib.load().vx_na3d_tiling
+    fn.argtypes = [ctypes.c_int32] * 7 + [ctypes.POINTER(ctypes.c_int32 * 3),
+                                          ctypes.POINTER(ctypes.c_int32),
+                                          ctypes.POINTER(ctypes.c_int32 * 3)]
+    fn.restype = ctypes.c_int
+    _lib.check(fn(*[int(x) for x in grid], *[int(x) for x in kernel_size], int(head_dim),
+                  ctypes.byref(qb), ctypes.byref(pair), ctypes.byref(kv)))
+    return {"q_box": tuple(qb), "pair": ("t", "h", "w", "heads")[pair.value],
+            "kv_tile": tuple(kv)}
+
+
 def window_start(length: int, kernel: int) -> np.ndarray:
     """Per-index window start along one axis, computed by the library
     (the `_window_start` contract, diffusion_vae.py:152-164)."""
