@@ -239,3 +239,38 @@ def test_axis_exchange_mode():
         ulysses.register_axis("xchg_test", None, exchange="mpi")
     ulysses.unregister_axis("xchg_test")
     assert ulysses._exchange("xchg_test") == "nccl"
+
+
+def test_peer_workspace_layout():
+    """The peer exchange's slab layout: slice j of a slab is a contiguous
+    block of (prefix + P * S_loc) rows x hs heads; in it, rank r's chunk
+    starts at row prefix + r * S_loc; the chunks of all ranks and slices
+    tile the slab exactly once (so no two ranks' stores overlap)."""
+    from vidax_b200.ulysses import _pieces
+    from vidax_b200.ulysses_peer import PeerWorkspace
+    for P, S_loc, H, D, prefix in [(2, 96, 5, 64, 0), (8, 40, 12, 128, 0), (4, 24, 6, 128, 17)]:
+        Hg = -(-H // P)
+        owners = {}
+        for r in range(P):
+            ws = object.__new__(PeerWorkspace)
+            ws.P, ws.rank, ws.seq_local, ws.heads, ws.head_dim = P, r, S_loc, H, D
+            ws.prefix, ws.Hg = prefix, Hg
+            ws.slab_bytes = ((prefix + P * S_loc) * Hg * D * 2 + 255) // 256 * 256
+            ws.base = [g * 10 ** 9 for g in range(P)]
+            sizes = _pieces(Hg)
+            offs = [sum(sizes[:j]) for j in range(len(sizes))]
+            for hs, off in zip(sizes, offs):
+                for g in range(P):
+                    addr = ws.remote(g, 1, off, hs)
+                    rel = addr - ws.base[g] - ws.slab_bytes
+                    assert rel % (hs * D * 2) == 0
+                    start = rel // 2
+                    for e in range(start, start + S_loc * hs * D, D):
+                        assert (g, e) not in owners, (P, r, g, e)
+                        owners[(g, e)] = r
+                    assert ws.remote_prefix(g, 1, off) == ws.base[g] + ws.slab_bytes + 2 * (
+                        prefix + P * S_loc) * off * D
+        # every rank-g slab row-head vector outside the prefix has exactly one writer
+        for g in range(P):
+            mine = sorted(e for (gg, e) in owners if gg == g)
+            assert len(mine) == P * S_loc * Hg, (len(mine), P * S_loc * Hg)
